@@ -1,0 +1,259 @@
+// fp8imma C++ API and C ABI (include/fp8imma/imma_fp8.h, fp8imma_ext.h).
+//
+// Host-side dispatch: validate, pick a kernel family for the shape, launch on
+// the caller's stream. Mirrors the reference launchers in
+// src/fp8imma/imma_fp8_v{2,3,4,4_texscale}.cu and the C wrappers in
+// src/fp8imma/impl/cabi_wrappers.inl (same names, argument order, return
+// codes).
+#include "fp8imma/fp8imma_ext.h"
+#include "fp8imma/imma_fp8.h"
+#include "fp8imma_kernels.h"
+
+#include <atomic>
+#include <mutex>
+#include <set>
+#include <utility>
+
+namespace fp8imma_b200 {
+
+namespace {
+std::atomic<int> g_splitk{0};
+std::atomic<int> g_small_m_max{64};
+thread_local int t_last_path = 0;
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+enum { FMT_E4M3_REF = 0, FMT_E5M2 = 1 };
+}  // namespace
+
+cudaError_t ensure_smem_attr(const void* kernel, int bytes) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(mu);
+  auto key = std::make_pair(kernel, dev);
+  if (done.count(key)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (e == cudaSuccess) done.insert(key);
+  return e;
+}
+
+int num_sms_current() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cache[dev] = v;
+  }
+  return cache[dev];
+}
+
+// One reference-semantics int8 GEMM. `group` is the activation load group
+// of the reference variant (8 for v4, 16 for v2/v3).
+static cudaError_t run_int8(GemvParams p, int a_type, int fmt, int group, cudaStream_t stream) {
+  t_last_path = 0;
+  if (p.M <= 0 || p.N <= 0) return cudaErrorInvalidConfiguration;
+  if (p.K < 0 || !p.A || !p.B || !p.D || (!p.scale_u16 && !p.scale_tex)) return cudaErrorInvalidValue;
+  p.keff_a = p.K - p.K % group;
+  const bool fast_shape = p.K > 0 && (p.K % 16) == 0 && aligned16(p.A) && aligned16(p.B);
+  if (fast_shape) {
+    t_last_path = 1;
+    return launch_gemv_s8(p, a_type, fmt, g_splitk.load(), stream);
+  }
+  t_last_path = 2;
+  return launch_generic_s8(p, a_type, fmt, stream);
+}
+
+static GemvParams base_params(const void* A, const void* B, const void* scales, unsigned long long tex,
+                              void* D, int M, int N, int K, float global_scale, float a_inv_scale) {
+  GemvParams p = {};
+  p.A = A;
+  p.B = static_cast<const uint8_t*>(B);
+  p.scale_u16 = static_cast<const uint16_t*>(scales);
+  p.scale_tex = tex;
+  p.D = D;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.global_scale = global_scale;
+  // the reference converts a_inv_scale to fp16 once on the host (imma_fp8_v4.cu:38)
+  p.a_inv_h = __half_as_ushort(__float2half(a_inv_scale));
+  return p;
+}
+
+static int ref_launch(int kChunk, int a_type, int group, const void* A, const void* B, const void* scales,
+                      unsigned long long tex, void* D, int M, int N, int K, float gs, float ainv,
+                      void* stream) {
+  if (kChunk != 32 && kChunk != 64) return (int)cudaErrorInvalidValue;
+  GemvParams p = base_params(A, B, scales, tex, D, M, N, K, gs, ainv);
+  return (int)run_int8(p, a_type, FMT_E4M3_REF, group, static_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------------------- extended GEMM ----
+
+static cudaError_t gemm_ex(const fp8imma_gemm_args* a, cudaStream_t stream) {
+  t_last_path = 0;
+  if (!a) return cudaErrorInvalidValue;
+  if (a->path != FP8IMMA_PATH_INT8_EXACT) return cudaErrorNotSupported;
+  if (a->a_type < 0 || a->a_type > 2 || a->b_format < 0 || a->b_format > 1) return cudaErrorInvalidValue;
+  if (a->out_type < 0 || a->out_type > 1 || a->out_layout < 0 || a->out_layout > 1) return cudaErrorInvalidValue;
+  if (a->act_quant < 0 || a->act_quant > 1) return cudaErrorInvalidValue;
+  if (a->act_quant == FP8IMMA_AQ_ROW && a->a_type == FP8IMMA_A_S8) return cudaErrorInvalidValue;
+  GemvParams p = base_params(a->A, a->B, a->col_scales_u16, 0ull, a->D, a->M, a->N, a->K,
+                             a->global_scale, a->a_inv_scale);
+  p.col_scale_f32 = a->col_scales_f32;
+  p.acc_out = a->acc_out;
+  p.out_bf16 = a->out_type;
+  p.out_row_major = a->out_layout;
+  const int group = a->a_type == FP8IMMA_A_S8 ? 16 : 8;
+  if (a->act_quant == FP8IMMA_AQ_ROW) {
+    if (a->M <= 0 || a->N <= 0) return cudaErrorInvalidConfiguration;
+    if (!a->A || a->K < 0) return cudaErrorInvalidValue;
+    void* tmp = nullptr;
+    size_t bytes = (size_t)a->M * (sizeof(float) + sizeof(uint16_t)) + 16;
+    cudaError_t e = cudaMallocAsync(&tmp, bytes, stream);
+    if (e != cudaSuccess) return e;
+    float* g = static_cast<float*>(tmp);
+    uint16_t* inv = reinterpret_cast<uint16_t*>(g + a->M);
+    e = launch_row_scales(a->A, a->a_type, a->M, a->K, inv, g, stream);
+    if (e == cudaSuccess) {
+      p.row_inv_h = inv;
+      p.row_g = g;
+      e = run_int8(p, a->a_type, a->b_format, group, stream);
+    }
+    cudaError_t e2 = cudaFreeAsync(tmp, stream);
+    return e != cudaSuccess ? e : e2;
+  }
+  return run_int8(p, a->a_type, a->b_format, group, stream);
+}
+
+}  // namespace fp8imma_b200
+
+using namespace fp8imma_b200;
+
+// ------------------------------------------------------------ C++ API -----
+namespace fp8imma {
+
+void init_fp8_e4m3_lut() {}
+
+cudaError_t launch_imma_fp8_jit_v2(int kChunk, const int8_t* A, const uint8_t* B, const uint16_t* s,
+                                   half* D, int M, int N, int K, float gs, cudaStream_t st) {
+  return (cudaError_t)ref_launch(kChunk, A_S8, 16, A, B, s, 0ull, D, M, N, K, gs, 1.0f, st);
+}
+cudaError_t launch_imma_fp8_jit_v2_i8lut(int kChunk, const int8_t* A, const uint8_t* B,
+                                         const uint16_t* s, half* D, int M, int N, int K, float gs,
+                                         cudaStream_t st) {
+  return (cudaError_t)ref_launch(kChunk, A_S8, 16, A, B, s, 0ull, D, M, N, K, gs, 1.0f, st);
+}
+cudaError_t launch_imma_fp8_actquant_v3_f16(int kChunk, const half* A, const uint8_t* B,
+                                            const uint16_t* s, half* D, int M, int N, int K,
+                                            float gs, float ainv, cudaStream_t st) {
+  return (cudaError_t)ref_launch(kChunk, A_F16, 16, A, B, s, 0ull, D, M, N, K, gs, ainv, st);
+}
+cudaError_t launch_imma_fp8_actquant_v3_bf16(int kChunk, const __nv_bfloat16* A, const uint8_t* B,
+                                             const uint16_t* s, half* D, int M, int N, int K,
+                                             float gs, float ainv, cudaStream_t st) {
+  return (cudaError_t)ref_launch(kChunk, A_BF16, 16, A, B, s, 0ull, D, M, N, K, gs, ainv, st);
+}
+cudaError_t launch_imma_fp8_actquant_v4_f16(int kChunk, const half* A, const uint8_t* B,
+                                            const uint16_t* s, half* D, int M, int N, int K,
+                                            float gs, float ainv, cudaStream_t st) {
+  return (cudaError_t)ref_launch(kChunk, A_F16, 8, A, B, s, 0ull, D, M, N, K, gs, ainv, st);
+}
+cudaError_t launch_imma_fp8_actquant_v4_bf16(int kChunk, const __nv_bfloat16* A, const uint8_t* B,
+                                             const uint16_t* s, half* D, int M, int N, int K,
+                                             float gs, float ainv, cudaStream_t st) {
+  return (cudaError_t)ref_launch(kChunk, A_BF16, 8, A, B, s, 0ull, D, M, N, K, gs, ainv, st);
+}
+cudaError_t launch_imma_fp8_actquant_v4_texscale_f16(int kChunk, const half* A, const uint8_t* B,
+                                                     cudaTextureObject_t tex, half* D, int M, int N,
+                                                     int K, float gs, float ainv, cudaStream_t st) {
+  if (tex == 0) return cudaErrorInvalidValue;
+  return (cudaError_t)ref_launch(kChunk, A_F16, 8, A, B, nullptr, (unsigned long long)tex, D, M, N, K,
+                                 gs, ainv, st);
+}
+cudaError_t launch_imma_fp8_actquant_v4_texscale_bf16(int kChunk, const __nv_bfloat16* A,
+                                                      const uint8_t* B, cudaTextureObject_t tex,
+                                                      half* D, int M, int N, int K, float gs,
+                                                      float ainv, cudaStream_t st) {
+  if (tex == 0) return cudaErrorInvalidValue;
+  return (cudaError_t)ref_launch(kChunk, A_BF16, 8, A, B, nullptr, (unsigned long long)tex, D, M, N, K,
+                                 gs, ainv, st);
+}
+
+}  // namespace fp8imma
+
+// --------------------------------------------------------------- C ABI -----
+extern "C" {
+
+void fp8imma_init_fp8_e4m3_lut(void) { fp8imma::init_fp8_e4m3_lut(); }
+
+int fp8imma_launch_imma_fp8_jit_v2(int kChunk, const void* A, const void* B, const void* s, void* D,
+                                   int M, int N, int K, float gs, void* stream) {
+  return ref_launch(kChunk, A_S8, 16, A, B, s, 0ull, D, M, N, K, gs, 1.0f, stream);
+}
+int fp8imma_launch_imma_fp8_jit_v2_i8lut(int kChunk, const void* A, const void* B, const void* s,
+                                         void* D, int M, int N, int K, float gs, void* stream) {
+  return ref_launch(kChunk, A_S8, 16, A, B, s, 0ull, D, M, N, K, gs, 1.0f, stream);
+}
+int fp8imma_launch_imma_fp8_actquant_v3_f16(int kChunk, const void* A, const void* B, const void* s,
+                                            void* D, int M, int N, int K, float gs, float ainv,
+                                            void* stream) {
+  return ref_launch(kChunk, A_F16, 16, A, B, s, 0ull, D, M, N, K, gs, ainv, stream);
+}
+int fp8imma_launch_imma_fp8_actquant_v3_bf16(int kChunk, const void* A, const void* B, const void* s,
+                                             void* D, int M, int N, int K, float gs, float ainv,
+                                             void* stream) {
+  return ref_launch(kChunk, A_BF16, 16, A, B, s, 0ull, D, M, N, K, gs, ainv, stream);
+}
+int fp8imma_launch_imma_fp8_actquant_v4_texscale_f16(int kChunk, const void* A, const void* B,
+                                                     void* tex, void* D, int M, int N, int K,
+                                                     float gs, float ainv, void* stream) {
+  if (!tex) return (int)cudaErrorInvalidValue;
+  return ref_launch(kChunk, A_F16, 8, A, B, nullptr, (unsigned long long)(uintptr_t)tex, D, M, N, K, gs,
+                    ainv, stream);
+}
+int fp8imma_launch_imma_fp8_actquant_v4_texscale_bf16(int kChunk, const void* A, const void* B,
+                                                      void* tex, void* D, int M, int N, int K,
+                                                      float gs, float ainv, void* stream) {
+  if (!tex) return (int)cudaErrorInvalidValue;
+  return ref_launch(kChunk, A_BF16, 8, A, B, nullptr, (unsigned long long)(uintptr_t)tex, D, M, N, K, gs,
+                    ainv, stream);
+}
+int fp8imma_launch_imma_fp8_actquant_v4_f16(int kChunk, const void* A, const void* B, const void* s,
+                                            void* D, int M, int N, int K, float gs, float ainv,
+                                            void* stream) {
+  return ref_launch(kChunk, A_F16, 8, A, B, s, 0ull, D, M, N, K, gs, ainv, stream);
+}
+int fp8imma_launch_imma_fp8_actquant_v4_bf16(int kChunk, const void* A, const void* B, const void* s,
+                                             void* D, int M, int N, int K, float gs, float ainv,
+                                             void* stream) {
+  return ref_launch(kChunk, A_BF16, 8, A, B, s, 0ull, D, M, N, K, gs, ainv, stream);
+}
+
+int fp8imma_gemm(const fp8imma_gemm_args* args, void* stream) {
+  return (int)gemm_ex(args, static_cast<cudaStream_t>(stream));
+}
+
+int fp8imma_set_splitk(int splits) {
+  if (splits != 0 && splits != 1 && splits != 2 && splits != 4 && splits != 8) return (int)cudaErrorInvalidValue;
+  g_splitk.store(splits);
+  return 0;
+}
+
+int fp8imma_set_small_m_max(int m) {
+  if (m < 0) return (int)cudaErrorInvalidValue;
+  g_small_m_max.store(m);
+  return 0;
+}
+
+int fp8imma_last_path(void) { return t_last_path; }
+
+const char* fp8imma_version(void) { return "fp8imma-b200 0.1 (sm_100a)"; }
+
+}  // extern "C"

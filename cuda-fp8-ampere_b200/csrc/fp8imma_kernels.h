@@ -1,0 +1,50 @@
+// Internal launch interface between the C ABI (api.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace fp8imma_b200 {
+
+enum { A_F16 = 0, A_BF16 = 1, A_S8 = 2 };
+
+// Arguments of one reference-exact int8 GEMM launch (small-M split-K path,
+// generic path). Layouts as in the reference API: A [M,K] row-major,
+// B [N,K] row-major ("col-major KxN"), D col-major [N,M] unless out_row_major.
+struct GemvParams {
+  const void* A;
+  const uint8_t* B;
+  const uint16_t* scale_u16;        // [N] fp16 bits (ignored when use_tex)
+  unsigned long long scale_tex;     // cudaTextureObject_t over u16 scale bits (0: none)
+  void* D;
+  int32_t* acc_out;                 // optional [N,M] int32 accumulators
+  const uint16_t* row_inv_h;        // optional per-row fp16 a_inv (row quant)
+  const float* row_g;               // optional per-row global scale (row quant)
+  const float* col_scale_f32;       // optional [N] fp32 extra column scale
+  int M, N, K;
+  int k_per_cta;                    // filled by the launcher
+  int kc;                           // activation chunk staged in shared memory
+  int keff_a;                       // generic path: A elements with k >= keff_a read 0
+  float global_scale;
+  uint16_t a_inv_h;                 // per-tensor activation multiplier (fp16 bits)
+  int out_bf16;
+  int out_row_major;
+};
+
+cudaError_t ensure_smem_attr(const void* kernel, int bytes);
+int num_sms_current();
+
+// Small-M split-K kernel (requires K % 16 == 0, 16-byte aligned A/B rows).
+// splits = 0 picks the K split from the shape.
+cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaStream_t stream);
+int gemv_pick_splits(int N, int K, int mchunks, int num_sms);
+
+// Exact fallback for shapes the fast kernels do not take (any K, any alignment).
+cudaError_t launch_generic_s8(const GemvParams& p, int a_type, int fmt, cudaStream_t stream);
+
+// Per-row dynamic activation scales: a_inv_h[m] (fp16 bits), g[m] (fp32).
+cudaError_t launch_row_scales(const void* A, int a_type, int M, int K, uint16_t* a_inv_h,
+                              float* g, cudaStream_t stream);
+
+}  // namespace fp8imma_b200

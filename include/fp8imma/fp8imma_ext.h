@@ -1,0 +1,83 @@
+// fp8imma extension C ABI — B200 (sm_100a).
+//
+// Entry points for features the reference API (imma_fp8.h) has no slot for:
+// per-row dynamic activation quantisation, an fp32 per-column scale fused
+// into the epilogue, bf16 output, row-major output, E5M2 weight storage, the
+// native FP8 tensor-core path, an int32 accumulator export, and the fp8wgt
+// torch extension's fp16-activation kernel as a C entry point.
+// Same conventions as the reference C ABI: plain pointers, void* stream
+// (cudaStream_t), int return = cudaError_t (0 = success); the library
+// launches asynchronously on the caller's stream.
+#pragma once
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum fp8imma_a_type { FP8IMMA_A_F16 = 0, FP8IMMA_A_BF16 = 1, FP8IMMA_A_S8 = 2 };
+
+// B byte format. On the int8-exact path E4M3 decodes through the reference
+// table semantics (exponent 15: +-Inf for mantissa 0, NaN otherwise); on the
+// native path E4M3 is the hardware E4M3FN format. E5M2 is IEEE-like on both.
+enum fp8imma_b_format { FP8IMMA_B_E4M3 = 0, FP8IMMA_B_E5M2 = 1 };
+
+enum fp8imma_path {
+  FP8IMMA_PATH_INT8_EXACT = 0,  // reference arithmetic, bit-exact int32 accumulators
+  FP8IMMA_PATH_FP8_NATIVE = 1   // activations -> E4M3 per row, FP8 tensor cores, fp32 accumulate
+};
+
+enum fp8imma_act_quant {
+  FP8IMMA_AQ_TENSOR = 0,  // one a_inv_scale / global_scale for the tensor (reference behaviour)
+  FP8IMMA_AQ_ROW = 1      // per-row absmax: a_inv_m = 127/absmax_m, g_m = 1/a_inv_m
+};
+
+enum fp8imma_out_type { FP8IMMA_OUT_F16 = 0, FP8IMMA_OUT_BF16 = 1 };
+enum fp8imma_out_layout { FP8IMMA_OUT_COL = 0 /* D[n*M+m] */, FP8IMMA_OUT_ROW = 1 /* D[m*N+n] */ };
+
+typedef struct fp8imma_gemm_args {
+  int path;        // fp8imma_path
+  int a_type;      // fp8imma_a_type (S8 only on the int8-exact path)
+  int b_format;    // fp8imma_b_format
+  int act_quant;   // fp8imma_act_quant (int8-exact path; the native path is always per row)
+  int out_type;    // fp8imma_out_type
+  int out_layout;  // fp8imma_out_layout
+  int M, N, K;
+  const void* A;               // [M,K] row-major
+  const void* B;               // [N,K] row-major FP8 bytes
+  const void* col_scales_u16;  // int8-exact path: [N] fp16 int8-step scales (required)
+  const float* col_scales_f32; // optional [N] fp32 multiplier (sigma_c); native path: weight scale
+  float global_scale;          // int8-exact path with FP8IMMA_AQ_TENSOR
+  float a_inv_scale;           // int8-exact path with FP8IMMA_AQ_TENSOR
+  void* D;                     // output, out_type / out_layout
+  int32_t* acc_out;            // optional [N,M] int32 accumulators (int8-exact path)
+} fp8imma_gemm_args;
+
+// Extended GEMM. No reference counterpart (extends imma_fp8.h:230). On the
+// int8-exact path with act_quant = TENSOR, out F16/COL, no col_scales_f32 it
+// equals fp8imma_launch_imma_fp8_actquant_v4_{f16,bf16} bit for bit.
+// Per-row quantisation and the native path use stream-ordered temporary
+// buffers (cudaMallocAsync on `stream`).
+int fp8imma_gemm(const fp8imma_gemm_args* args, void* stream);
+
+// fp8wgt linear: C[M,N] (fp32, row-major) = A[M,K] (fp16) x decode(B[N,K])^T,
+// decode(b) = fp16_rn(float(lut_e4m3[b]) * scale_b). Replaces
+// torch_ext/fp8wgt/fp8wgt_ext_cuda.cu:223 fp8_linear_forward (kernel :135),
+// as a C entry point; runs on `stream` (the reference used the default stream).
+int fp8imma_fp8wgt_linear_forward(const void* A_f16, const void* B_u8, float scale_b, void* C_f32,
+                                  int M, int N, int K, void* stream);
+
+// Tuning / introspection (no reference counterpart).
+// Force the K split of the small-M kernel (0 = automatic; 1, 2, 4 or 8).
+int fp8imma_set_splitk(int splits);
+// Largest M routed to the small-M split-K kernel (default 64).
+int fp8imma_set_small_m_max(int m);
+// Kernel family the last fp8imma call on this thread launched:
+// 0 none, 1 small-M split-K, 2 generic fallback, 3 tcgen05 GEMM, 4 native FP8.
+int fp8imma_last_path(void);
+const char* fp8imma_version(void);
+
+#ifdef __cplusplus
+}  // extern "C"
+#endif

@@ -1,0 +1,100 @@
+"""GPU parity of the extension entry point fp8imma_gemm (int8-exact path):
+per-row activation quantisation, fp32 column scale, bf16 and row-major
+output, E5M2 weights, int32 accumulator export; and the fp8wgt linear."""
+import numpy as np
+import pytest
+import torch
+
+import fp8imma_b200 as F
+from helpers import bits_equal, to_np_bits
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def inputs(M, N, K, seed, a_bf16=False, fmt="e4m3"):
+    rng = np.random.default_rng(seed)
+    a = (rng.standard_normal((M, K)) * 2.0).astype(np.float32)
+    if a_bf16:
+        A = (a.view(np.uint32) >> 16).astype(np.uint16)
+    else:
+        A = a.astype(np.float16).view(np.uint16)
+    w = rng.standard_normal((N, K)).astype(np.float32) * 0.02
+    sig = np.abs(w).max(axis=1) / (448.0 if fmt == "e4m3" else 57344.0)
+    enc = O.e4m3fn_encode if fmt == "e4m3" else O.e5m2_encode
+    B = enc(w / sig[:, None])
+    s = rng.uniform(0.5, 3.5, N).astype(np.float16).view(np.uint16)
+    return A, B, s, sig.astype(np.float32)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 512), (16, 4096, 1024), (37, 300, 256), (64, 128, 2048)])
+@pytest.mark.parametrize("a_bf16", [False, True])
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+@pytest.mark.parametrize("row_quant", [False, True])
+def test_gemm_ex_matches_oracle(cuda, M, N, K, a_bf16, fmt, row_quant):
+    e = F.ext()
+    A, B, s, sig = inputs(M, N, K, seed=M + N + K, a_bf16=a_bf16, fmt=fmt)
+    b_fmt = O.FMT_E5M2 if fmt == "e5m2" else O.FMT_E4M3_REF
+    D_o, acc_o = O.gemm_ex(A, B, s, a_bf16=a_bf16, b_fmt=b_fmt, row_quant=row_quant, col_scale_f32=sig,
+                           global_scale=0.05, a_inv_scale=20.0, out_bf16=a_bf16, out_row_major=a_bf16,
+                           nthreads=8)
+    dA = torch.from_numpy(A.view(np.int16)).cuda().view(torch.bfloat16 if a_bf16 else torch.float16)
+    D, acc = e.imma_fp8_gemm(dA, torch.from_numpy(B).cuda(), torch.from_numpy(s.view(np.int16)).cuda(),
+                             torch.from_numpy(sig).cuda(), 0.05, 20.0, "row" if row_quant else "tensor", fmt, "int8",
+                             "bfloat16" if a_bf16 else "float16", "row" if a_bf16 else "col", True, None)
+    torch.cuda.synchronize()
+    assert (acc.cpu().numpy() == acc_o).all(), "int32 accumulators differ"
+    assert bits_equal(to_np_bits(D), D_o, is_bf16=a_bf16).all()
+
+
+def test_gemm_ex_default_equals_reference_api(cuda):
+    e = F.ext()
+    A, B, s, _ = inputs(16, 512, 1024, seed=1)
+    dA = torch.from_numpy(A.view(np.int16)).cuda().view(torch.float16)
+    dB = torch.from_numpy(B).cuda()
+    ds = torch.from_numpy(s.view(np.int16)).cuda()
+    D1 = e.imma_fp8_v4_act(dA, dB, ds.view(torch.float16), 0.3, 7.0, 32)
+    D2, _ = e.imma_fp8_gemm(dA, dB, ds, None, 0.3, 7.0, "tensor", "e4m3", "int8", "float16", "col", False, None)
+    assert torch.equal(D1.view(torch.int16), D2.view(torch.int16))
+
+
+def test_int8_activation_api(cuda):
+    e = F.ext()
+    rng = np.random.default_rng(4)
+    A = rng.integers(-128, 128, (8, 256), dtype=np.int8)
+    _, B, s, _ = inputs(8, 64, 256, seed=4)
+    D_o, acc_o = O.gemm_ex(A, B, s, global_scale=0.01)
+    D, acc = e.imma_fp8_gemm(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(),
+                             torch.from_numpy(s.view(np.int16)).cuda(), None, 0.01, 1.0, "tensor", "e4m3", "int8",
+                             "float16", "col", True, None)
+    assert (acc.cpu().numpy() == acc_o).all()
+    assert bits_equal(to_np_bits(D), D_o).all()
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 64, 64), (32, 256, 512), (64, 128, 1024), (48, 80, 96)])
+def test_fp8wgt_linear(cuda, M, N, K):
+    w = F.wgt_ext()
+    rng = np.random.default_rng(M * N)
+    A = (rng.standard_normal((M, K))).astype(np.float16)
+    B = rng.integers(0, 0x78, (N, K), dtype=np.uint8)   # finite codes
+    B |= (rng.integers(0, 2, (N, K), dtype=np.uint8) << 7)
+    C_o = O.fp8wgt(A.view(np.uint16), B, 0.05)
+    C = w.fp8_linear_forward(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), 0.05)
+    torch.cuda.synchronize()
+    C = C.cpu().numpy()
+    assert C.shape == (M, N) and C.dtype == np.float32
+    # fp32 accumulation in a different order: relative tolerance on the output scale
+    err = np.abs(C - C_o).max() / max(np.abs(C_o).max(), 1e-6)
+    assert err < 1e-3, err
+
+
+def test_fp8linear_module(cuda):
+    import fp8_linear
+
+    rng = np.random.default_rng(0)
+    B = torch.from_numpy(rng.integers(0, 0x70, (128, 256), dtype=np.uint8)).cuda()
+    mod = fp8_linear.FP8Linear(B, 0.1)
+    A = torch.randn(32, 256, device="cuda", dtype=torch.float16)
+    out = mod(A)
+    C_o = O.fp8wgt(A.cpu().numpy().view(np.uint16), B.cpu().numpy(), 0.1)
+    assert np.abs(out.cpu().numpy() - C_o).max() / np.abs(C_o).max() < 1e-3
