@@ -195,6 +195,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-lib", action="store_true")
     ap.add_argument("--points", action="store_true", help="also time the other decode/70B shapes")
+    ap.add_argument("--pdl", action="store_true", help="launch with programmatic dependent launch")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     w = WORKLOADS[args.workload]
@@ -217,6 +218,7 @@ def main():
     from fp8imma_b200 import workloads as WL
 
     ext = F.ext()
+    F.lib().fp8imma_set_pdl(1 if args.pdl else 0)
     M, Nl, K = w["M"], w["N"], w["K"]
     N_tot = Nl * world
     B, s16, sig = WL.make_weights(Nl, K, w["sigma_w"], "e4m3", seed=rank, device="cuda")
@@ -366,7 +368,8 @@ def main():
                        "weights": "E4M3 bytes, sigma_w=%g, per-column scales" % w["sigma_w"],
                        "path": "int8-exact (reference v4 semantics)", "parallelism": "column-parallel x%d" % world,
                        "l2": "weights rotated over %d copies (%.0f MB > 2x L2)" % (copies, copies * wbytes / 1e6),
-                       "timing": "CUDA graph of K steps" if world == 1 else "eager, NCCL all-gather in step"},
+                       "timing": "CUDA graph of K steps" if world == 1 else "eager, NCCL all-gather in step",
+                       "pdl": bool(args.pdl)},
             "tflops": round(tflops, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "traffic": traffic,
@@ -376,6 +379,7 @@ def main():
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": M * K * 2,
                     "d2h_bytes_per_step": Nl * M * 2},
             "gpu_launches": args.steps, "kernel_path": path_id, "clocks": clocks,
+            "device_error": int(F.lib().fp8imma_device_error(0)),
         }
         line.update(extra)
         print(json.dumps(line), flush=True)

@@ -30,7 +30,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
               "--expt-relaxed-constexpr", "-I" + INCLUDE, "-I" + CSRC]
 
-CU_SOURCES = ["api.cu", "gemv_splitk.cu", "generic.cu", "fp8wgt.cu"]
+CU_SOURCES = ["api.cu", "gemv_splitk.cu", "generic.cu", "fp8wgt.cu", "host_util.cu"]
 
 
 def _run(cmd: list[str]) -> None:
@@ -68,7 +68,7 @@ def build_lib(force: bool = False, extra_flags: list[str] | None = None) -> str:
     with cf.ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as ex:
         list(ex.map(_run, jobs))
     if force or jobs or not _newer(LIB, objs):
-        _run([NVCC] + ARCH + ["-shared", "-Xcompiler", "-fPIC", "-o", LIB] + objs + ["-lcudart", "-lcuda"])
+        _run([NVCC] + ARCH + ["-shared", "-Xcompiler", "-fPIC", "-o", LIB] + objs + ["-lcudart"])
     return LIB
 
 

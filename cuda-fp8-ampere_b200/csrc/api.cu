@@ -19,6 +19,7 @@ namespace fp8imma_b200 {
 namespace {
 std::atomic<int> g_splitk{0};
 std::atomic<int> g_small_m_max{64};
+std::atomic<int> g_pdl{0};
 thread_local int t_last_path = 0;
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -60,6 +61,7 @@ static cudaError_t run_int8(GemvParams p, int a_type, int fmt, int group, cudaSt
   if (p.M <= 0 || p.N <= 0) return cudaErrorInvalidConfiguration;
   if (p.K < 0 || !p.A || !p.B || !p.D || (!p.scale_u16 && !p.scale_tex)) return cudaErrorInvalidValue;
   p.keff_a = p.K - p.K % group;
+  p.pdl = g_pdl.load();
   const bool fast_shape = p.K > 0 && (p.K % 16) == 0 && aligned16(p.A) && aligned16(p.B);
   if (fast_shape) {
     t_last_path = 1;
@@ -253,6 +255,13 @@ int fp8imma_set_small_m_max(int m) {
 }
 
 int fp8imma_last_path(void) { return t_last_path; }
+
+int fp8imma_set_pdl(int enable) {
+  g_pdl.store(enable ? 1 : 0);
+  return 0;
+}
+
+unsigned int fp8imma_device_error(int clear) { return gemv_device_error(clear != 0); }
 
 const char* fp8imma_version(void) { return "fp8imma-b200 0.1 (sm_100a)"; }
 

@@ -1,6 +1,7 @@
 // Internal launch interface between the C ABI (api.cu) and the kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
@@ -30,9 +31,17 @@ struct GemvParams {
   uint16_t a_inv_h;                 // per-tensor activation multiplier (fp16 bits)
   int out_bf16;
   int out_row_major;
+  int pdl;                          // launched with programmatic stream serialisation
 };
 
 cudaError_t ensure_smem_attr(const void* kernel, int bytes);
+
+// TMA descriptor for a 2-D byte tensor [outer][inner] (row pitch row_bytes).
+cudaError_t make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                            uint32_t box_inner, uint32_t box_outer, bool swizzle128);
+
+// Device error words of the kernel files that wait on barriers (0 = none).
+unsigned int gemv_device_error(bool clear);
 int num_sms_current();
 
 // Small-M split-K kernel (requires K % 16 == 0, 16-byte aligned A/B rows).

@@ -1,23 +1,30 @@
-// Split-K "skinny" GEMM for small M (decode shapes), reference-exact int8 path.
+// Split-K skinny GEMM for small M (decode shapes), reference-exact int8 path.
 //
-// Work split (B200): a CTA owns 128 weight columns and one K-slice; the
-// K-slices of one column tile form a thread-block cluster and reduce their
-// int32 partials through distributed shared memory, so no global scratch is
-// needed. Each warp owns 16 weight columns and streams them with 128-bit
-// non-allocating loads (16 contiguous K bytes per lane), transcodes the FP8
-// bytes to int8 in registers (fp8imma_device.cuh) and feeds them straight into
-// mma.sync m16n8k32 s8 as the A operand, with the quantised activations (from
-// shared memory) as the B operand. Within a 64-byte K block the physical MMA
-// k index is a permutation of the logical k; the same permutation is applied
-// to both operands, and int32 sums do not depend on order, so the result is
-// exact.
+// Work split (B200):
+//   * a CTA owns 128 weight columns and one K-slice; the K-slices of a column
+//     tile form a thread-block cluster and reduce their int32 partials through
+//     distributed shared memory (no global scratch);
+//   * one producer warp streams the weight tile with 2-D TMA loads
+//     (128 columns x 128 K-bytes = 16 KB per stage, 128-byte swizzle, 4-stage
+//     mbarrier ring), so the HBM stream is deep and costs no registers;
+//   * eight consumer warps each own 16 columns: 16-byte conflict-free shared
+//     loads, FP8 -> int8 transcode in registers (fp8imma_device.cuh), and
+//     mma.sync m16n8k32 s8 with the transcoded weights as the A operand and the
+//     quantised activations (shared memory) as the B operand.
+// Within each 64-byte K block the MMA's physical k index is a permutation of
+// the logical k; both operands use the same permutation and int32 sums do not
+// depend on order, so the result is exact. MMA rows map to tile columns
+// through sigma(g) = (g>>1) + 4*(g&1), which puts the two rows read by one
+// 8-lane shared-memory phase in different halves of the 128-byte swizzle
+// pattern (conflict-free).
 //
 // Reference counterpart: imma_gemm_fp8_actquant_cpasync_int8_colscale_fp16_
 // colmajor_kernel_v4 (src/fp8imma/impl/v4_kernels.inl:1-287), v3
-// (impl/v3_kernels.inl) and v2 (impl/v2_kernels.inl), which tile 64x64 and
-// waste 63/64 of their MMA rows at M=1.
-#include "fp8imma_kernels.h"
+// (impl/v3_kernels.inl) and v2 (impl/v2_kernels.inl): 64x64 tiles that waste
+// 63/64 of their MMA rows at M=1.
 #include "fp8imma_device.cuh"
+#include "fp8imma_kernels.h"
+#include "sm100_async.cuh"
 
 #include <cooperative_groups.h>
 
@@ -28,9 +35,15 @@ namespace fp8imma_b200 {
 
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kThreads = kConsumers + 32;  // + one TMA producer warp
 constexpr int kTileN = 128;
-constexpr int kUnroll = 4;  // 64-byte K blocks per register batch
+constexpr int kBlockK = 128;
+constexpr int kStages = 4;
+constexpr int kStageBytes = kTileN * kBlockK;
+constexpr int kBarOffset = kStages * kStageBytes;
+constexpr int kAqOffset = kBarOffset + 1024;
 
 __device__ __forceinline__ void mma_s8_16832(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                              uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -41,11 +54,12 @@ __device__ __forceinline__ void mma_s8_16832(int (&c)[4], uint32_t a0, uint32_t 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ float load_col_scale(const GemvParams& p, int n) {
-  uint16_t bits;
-  if (p.scale_tex) bits = tex1Dfetch<unsigned short>((cudaTextureObject_t)p.scale_tex, n);
-  else bits = p.scale_u16[n];
-  return __half2float(__ushort_as_half(bits));
+__device__ __forceinline__ uint4 lds128(const void* p) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "r"(smem_u32(p)));
+  return r;
 }
 
 __device__ __forceinline__ uint16_t load_col_scale_bits(const GemvParams& p, int n) {
@@ -53,14 +67,20 @@ __device__ __forceinline__ uint16_t load_col_scale_bits(const GemvParams& p, int
   return p.scale_u16[n];
 }
 
+template <int FMT, bool FAST>
+__device__ __forceinline__ uint32_t tc4(uint32_t x, uint32_t fscale, uint16_t inv_h) {
+  if (FAST) return FMT == FMT_E5M2 ? transcode4_fast_e5m2(x, fscale) : transcode4_fast_e4m3(x, fscale);
+  return transcode4_exact<FMT>(x, inv_h);
+}
+
 // Quantise A[m0 : m0+MR, k0 : k0+len] into aq (row stride `stride`), zero-
-// filling rows >= M and k >= kvalid.
+// filling rows >= M and k >= kvalid. Consumer threads only.
 template <int AT, int MR>
-__device__ __forceinline__ void quant_chunk(const GemvParams& p, int8_t* aq, int stride, int m0,
-                                            int k0, int len, int kvalid) {
+__device__ __forceinline__ void quant_chunk(const GemvParams& p, int8_t* aq, int stride, int m0, int k0, int len,
+                                            int kvalid) {
   const int items_per_row = len >> 3;  // 8 elements per item
   const int total = MR * items_per_row;
-  for (int it = threadIdx.x; it < total; it += kThreads) {
+  for (int it = threadIdx.x; it < total; it += kConsumers) {
     int r = it / items_per_row;
     int c = (it - r * items_per_row) << 3;
     int m = m0 + r, k = k0 + c;
@@ -86,100 +106,140 @@ __device__ __forceinline__ void quant_chunk(const GemvParams& p, int8_t* aq, int
   }
 }
 
-template <int AT, int MB, int FMT>
-__global__ void __launch_bounds__(kThreads, 2) gemv_s8_splitk_kernel(const __grid_constant__ GemvParams p) {
+template <int AT, int MB, int FMT, bool FAST>
+__device__ __forceinline__ void consumer_loop(const GemvParams& p, int (&acc)[MB][4], const uint8_t* stages,
+                                              uint64_t* full, uint64_t* empty, int8_t* aq, int astride, int m0,
+                                              int kbeg, int kend, int nkb, uint32_t fs0, uint32_t fs1, uint16_t inv0,
+                                              uint16_t inv1, int warp, int lane) {
   constexpr int MR = MB * 8;
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
+  const int rowA = warp * 16 + (g >> 1) + 4 * (g & 1);
+  const int rowB = rowA + 8;
+  const int swz = rowA & 7;  // == rowB & 7
+  int stage = 0;
+  uint32_t phase = 0;
+  bool ok = true;
+  for (int i = 0; i < nkb; ++i) {
+    const int koff = (i * kBlockK) % p.kc;
+    if (koff == 0) {
+      named_bar_sync(1, kConsumers);
+      int k0 = kbeg + i * kBlockK;
+      int len = min(p.kc, kend - k0);
+      len = (len + 63) & ~63;
+      quant_chunk<AT, MR>(p, aq, astride, m0, k0, len, kend);
+      named_bar_sync(1, kConsumers);
+    }
+    if (ok) ok = mbar_wait(&full[stage], phase, ERR_WAIT_FULL);
+    const uint8_t* st = stages + stage * kStageBytes;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = (4 * h + t) ^ swz;
+      uint4 w0 = lds128(st + rowA * kBlockK + (c << 4));
+      uint4 w1 = lds128(st + rowB * kBlockK + (c << 4));
+      uint32_t wa0 = tc4<FMT, FAST>(w0.x, fs0, inv0), wa1 = tc4<FMT, FAST>(w0.y, fs0, inv0);
+      uint32_t wa2 = tc4<FMT, FAST>(w0.z, fs0, inv0), wa3 = tc4<FMT, FAST>(w0.w, fs0, inv0);
+      uint32_t wb0 = tc4<FMT, FAST>(w1.x, fs1, inv1), wb1 = tc4<FMT, FAST>(w1.y, fs1, inv1);
+      uint32_t wb2 = tc4<FMT, FAST>(w1.z, fs1, inv1), wb3 = tc4<FMT, FAST>(w1.w, fs1, inv1);
+      const int8_t* arow = aq + koff + 64 * h + 16 * t;
+#pragma unroll
+      for (int nb = 0; nb < MB; ++nb) {
+        uint4 q = lds128(arow + (nb * 8 + g) * astride);
+        mma_s8_16832(acc[nb], wa0, wb0, wa1, wb1, q.x, q.y);
+        mma_s8_16832(acc[nb], wa2, wb2, wa3, wb3, q.z, q.w);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (++stage == kStages) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
+}
+
+template <int AT, int MB, int FMT>
+__global__ void __launch_bounds__(kThreads, 3)
+    gemv_s8_splitk_kernel(const __grid_constant__ GemvParams p, const __grid_constant__ CUtensorMap tmap) {
+  constexpr int MR = MB * 8;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOffset);
+  uint64_t* empty = full + kStages;
+  int8_t* aq = reinterpret_cast<int8_t*>(smem + kAqOffset);
+  int32_t* part = reinterpret_cast<int32_t*>(smem + kAqOffset);  // reused after the main loop
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int tile_n0 = blockIdx.x * kTileN;
   const int m0 = blockIdx.z * MR;
   const int kbeg = blockIdx.y * p.k_per_cta;
   const int kend = min(p.K, kbeg + p.k_per_cta);
+  const int nkb = kend > kbeg ? (kend - kbeg + kBlockK - 1) / kBlockK : 0;
   const int astride = p.kc + 64;  // +64 B: conflict-free 16-byte fragment loads
-  int8_t* aq = reinterpret_cast<int8_t*>(smem);
-  int32_t* part = reinterpret_cast<int32_t*>(smem);  // reused after the main loop
 
-  // ---- per-column constants (two columns per lane: rows g and g+8 of the MMA)
-  const int col0 = tile_n0 + warp * 16 + g, col1 = col0 + 8;
-  const bool ok0 = col0 < p.N, ok1 = col1 < p.N;
-  uint16_t inv0 = ok0 ? inv_scale_bits(load_col_scale_bits(p, col0)) : (uint16_t)0x3C00u;
-  uint16_t inv1 = ok1 ? inv_scale_bits(load_col_scale_bits(p, col1)) : (uint16_t)0x3C00u;
-  const bool fast0 = fast_ok<FMT>(inv0), fast1 = fast_ok<FMT>(inv1);
-  const uint32_t fs0 = fast_scale<FMT>(inv0), fs1 = fast_scale<FMT>(inv1);
-  const uint8_t* b0 = p.B + (size_t)(ok0 ? col0 : 0) * p.K + 16 * t;
-  const uint8_t* b1 = p.B + (size_t)(ok1 ? col1 : 0) * p.K + 16 * t;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (p.pdl) pdl_launch_dependents();
 
+  const int g = lane >> 2;
+  const int lc0 = warp * 16 + (g >> 1) + 4 * (g & 1);  // MMA rows g / g+8 -> tile columns lc0 / lc0+8
+  const bool consumer = warp < kConsumerWarps;
   int acc[MB][4];
 #pragma unroll
   for (int i = 0; i < MB; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0;
 
-  const int niter = kend > kbeg ? (kend - kbeg + 63) >> 6 : 0;
-  uint4 cur0[kUnroll], cur1[kUnroll];
-
-  auto load_batch = [&](uint4 (&d0)[kUnroll], uint4 (&d1)[kUnroll], int it0) {
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      int k = kbeg + ((it0 + u) << 6) + 16 * t;
-      bool kv = (it0 + u) < niter && k < kend;
-      d0[u] = (kv && ok0) ? ldg_stream_v4(b0 + (k - 16 * t)) : make_uint4(0u, 0u, 0u, 0u);
-      d1[u] = (kv && ok1) ? ldg_stream_v4(b1 + (k - 16 * t)) : make_uint4(0u, 0u, 0u, 0u);
-    }
-  };
-
-  load_batch(cur0, cur1, 0);
-  for (int it0 = 0; it0 < niter; it0 += kUnroll) {
-    const int koff = (it0 << 6) % p.kc;  // offset inside the current A chunk
-    if (koff == 0) {
-      __syncthreads();
-      int k0 = kbeg + (it0 << 6);
-      int len = min(p.kc, kend - k0);
-      len = (len + 63) & ~63;
-      quant_chunk<AT, MR>(p, aq, astride, m0, k0, len, kend);
-      __syncthreads();
-    }
-    uint4 nxt0[kUnroll], nxt1[kUnroll];
-    load_batch(nxt0, nxt1, it0 + kUnroll);
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      if (it0 + u < niter) {
-        uint32_t wa[4], wb[4];
-        wa[0] = transcode4<FMT>(cur0[u].x, fast0, fs0, inv0);
-        wa[1] = transcode4<FMT>(cur0[u].y, fast0, fs0, inv0);
-        wa[2] = transcode4<FMT>(cur0[u].z, fast0, fs0, inv0);
-        wa[3] = transcode4<FMT>(cur0[u].w, fast0, fs0, inv0);
-        wb[0] = transcode4<FMT>(cur1[u].x, fast1, fs1, inv1);
-        wb[1] = transcode4<FMT>(cur1[u].y, fast1, fs1, inv1);
-        wb[2] = transcode4<FMT>(cur1[u].z, fast1, fs1, inv1);
-        wb[3] = transcode4<FMT>(cur1[u].w, fast1, fs1, inv1);
-        const int8_t* arow = aq + koff + (u << 6) + 16 * t;
-#pragma unroll
-        for (int nb = 0; nb < MB; ++nb) {
-          uint4 q = *reinterpret_cast<const uint4*>(arow + (nb * 8 + g) * astride);
-          mma_s8_16832(acc[nb], wa[0], wb[0], wa[1], wb[1], q.x, q.y);
-          mma_s8_16832(acc[nb], wa[2], wb[2], wa[3], wb[3], q.z, q.w);
+  if (!consumer) {
+    // ---- TMA producer: weights are streamed from the first cycle (they do
+    // not depend on the previous kernel in the stream)
+    if (lane == 0) {
+      prefetch_tensormap(&tmap);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int i = 0; i < nkb; ++i) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY)) break;
+        mbar_arrive_expect_tx(&full[stage], kStageBytes);
+        tma_load_2d(stages + stage * kStageBytes, &tmap, &full[stage], kbeg + i * kBlockK, tile_n0);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
     }
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      cur0[u] = nxt0[u];
-      cur1[u] = nxt1[u];
-    }
+  } else {
+    const int col0 = tile_n0 + lc0, col1 = col0 + 8;
+    const bool ok0 = col0 < p.N, ok1 = col1 < p.N;
+    const uint16_t inv0 = ok0 ? inv_scale_bits(load_col_scale_bits(p, col0)) : (uint16_t)0x3C00u;
+    const uint16_t inv1 = ok1 ? inv_scale_bits(load_col_scale_bits(p, col1)) : (uint16_t)0x3C00u;
+    const bool all_fast = named_bar_and(2, kConsumers, fast_ok<FMT>(inv0) && fast_ok<FMT>(inv1));
+    if (p.pdl) pdl_wait();  // activations may come from the previous kernel
+    const uint32_t fs0 = fast_scale<FMT>(inv0), fs1 = fast_scale<FMT>(inv1);
+    if (all_fast)
+      consumer_loop<AT, MB, FMT, true>(p, acc, stages, full, empty, aq, astride, m0, kbeg, kend, nkb, fs0, fs1,
+                                       inv0, inv1, warp, lane);
+    else
+      consumer_loop<AT, MB, FMT, false>(p, acc, stages, full, empty, aq, astride, m0, kbeg, kend, nkb, fs0, fs1,
+                                        inv0, inv1, warp, lane);
   }
 
   // ---- partials -> shared memory, [128 cols][MR] int32
   __syncthreads();
-  {
-    const int r0 = warp * 16 + g;
+  if (consumer) {
+    const int t = lane & 3;
 #pragma unroll
     for (int nb = 0; nb < MB; ++nb) {
-      *reinterpret_cast<int2*>(part + r0 * MR + nb * 8 + 2 * t) = make_int2(acc[nb][0], acc[nb][1]);
-      *reinterpret_cast<int2*>(part + (r0 + 8) * MR + nb * 8 + 2 * t) = make_int2(acc[nb][2], acc[nb][3]);
+      *reinterpret_cast<int2*>(part + lc0 * MR + nb * 8 + 2 * t) = make_int2(acc[nb][0], acc[nb][1]);
+      *reinterpret_cast<int2*>(part + (lc0 + 8) * MR + nb * 8 + 2 * t) = make_int2(acc[nb][2], acc[nb][3]);
     }
   }
   cg::cluster_group cluster = cg::this_cluster();
   cluster.sync();
+  if (p.pdl) pdl_wait();  // outputs may still be read by the previous kernel
 
   // ---- cluster reduction + epilogue: CTA rank r finishes 128/S columns
   const int S = (int)cluster.num_blocks();
@@ -188,8 +248,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_s8_splitk_kernel(const __gri
   const int nelem = cols_per * MR;
   for (int e = threadIdx.x; e < nelem; e += kThreads) {
     int lc, mr;
-    if (p.out_row_major) { mr = e / cols_per; lc = rank * cols_per + (e - mr * cols_per); }
-    else { lc = rank * cols_per + e / MR; mr = e % MR; }
+    if (p.out_row_major) {
+      mr = e / cols_per;
+      lc = rank * cols_per + (e - mr * cols_per);
+    } else {
+      lc = rank * cols_per + e / MR;
+      mr = e % MR;
+    }
     int n = tile_n0 + lc, m = m0 + mr;
     int32_t s = 0;
     for (int q = 0; q < S; ++q) {
@@ -197,10 +262,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_s8_splitk_kernel(const __gri
       s += rp[lc * MR + mr];
     }
     if (n < p.N && m < p.M) {
-      float se = load_col_scale(p, n) * (p.row_g ? p.row_g[m] : p.global_scale);
+      float sc = __half2float(__ushort_as_half(load_col_scale_bits(p, n)));
+      float se = sc * (p.row_g ? p.row_g[m] : p.global_scale);
       if (p.col_scale_f32) se = se * p.col_scale_f32[n];
-      float v = (float)s * se;
-      uint16_t o = store_val(v, p.out_bf16);
+      uint16_t o = store_val((float)s * se, p.out_bf16);
       uint16_t* D = static_cast<uint16_t*>(p.D);
       if (p.out_row_major) D[(size_t)m * p.N + n] = o;
       else D[(size_t)n * p.M + m] = o;
@@ -211,7 +276,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_s8_splitk_kernel(const __gri
 }
 
 template <int AT, int MB, int FMT>
-cudaError_t launch_t(const GemvParams& p, int S, int mchunks, size_t smem, cudaStream_t stream) {
+cudaError_t launch_t(const GemvParams& p, const CUtensorMap& tmap, int S, int mchunks, size_t smem,
+                     cudaStream_t stream) {
   auto kern = gemv_s8_splitk_kernel<AT, MB, FMT>;
   cudaError_t e = ensure_smem_attr((const void*)kern, (int)smem);
   if (e != cudaSuccess) return e;
@@ -220,23 +286,26 @@ cudaError_t launch_t(const GemvParams& p, int S, int mchunks, size_t smem, cudaS
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = S;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, p);
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, p, tmap);
 }
 
 template <int AT, int FMT>
-cudaError_t launch_mb(const GemvParams& p, int MB, int S, int mchunks, size_t smem, cudaStream_t st) {
+cudaError_t launch_mb(const GemvParams& p, const CUtensorMap& tmap, int MB, int S, int mchunks, size_t smem,
+                      cudaStream_t st) {
   switch (MB) {
-    case 1: return launch_t<AT, 1, FMT>(p, S, mchunks, smem, st);
-    case 2: return launch_t<AT, 2, FMT>(p, S, mchunks, smem, st);
-    case 3: return launch_t<AT, 3, FMT>(p, S, mchunks, smem, st);
-    default: return launch_t<AT, 4, FMT>(p, S, mchunks, smem, st);
+    case 1: return launch_t<AT, 1, FMT>(p, tmap, S, mchunks, smem, st);
+    case 2: return launch_t<AT, 2, FMT>(p, tmap, S, mchunks, smem, st);
+    case 3: return launch_t<AT, 3, FMT>(p, tmap, S, mchunks, smem, st);
+    default: return launch_t<AT, 4, FMT>(p, tmap, S, mchunks, smem, st);
   }
 }
 
@@ -258,20 +327,34 @@ cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaSt
   int kper = (p.K + S - 1) / S;
   kper = (kper + 255) & ~255;
   p.k_per_cta = kper;
-  const int kc_max = MR > 16 ? 1024 : 2048;
+  const int kc_max = MR > 16 ? 512 : 1024;
   p.kc = kper < kc_max ? kper : kc_max;
   size_t smem_a = (size_t)MR * (p.kc + 64);
   size_t smem_p = (size_t)kTileN * MR * 4;
-  size_t smem = smem_a > smem_p ? smem_a : smem_p;
+  size_t smem = (size_t)kAqOffset + (smem_a > smem_p ? smem_a : smem_p) + 1024;  // + alignment slack
+  CUtensorMap tmap;
+  cudaError_t e = make_tmap_2d_u8(&tmap, p.B, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)p.K, kBlockK, kTileN,
+                                  /*swizzle128=*/true);
+  if (e != cudaSuccess) return e;
   switch (a_type * 3 + fmt) {
-    case A_F16 * 3 + FMT_E4M3_REF: return launch_mb<A_F16, FMT_E4M3_REF>(p, MB, S, mchunks, smem, stream);
-    case A_F16 * 3 + FMT_E5M2: return launch_mb<A_F16, FMT_E5M2>(p, MB, S, mchunks, smem, stream);
-    case A_BF16 * 3 + FMT_E4M3_REF: return launch_mb<A_BF16, FMT_E4M3_REF>(p, MB, S, mchunks, smem, stream);
-    case A_BF16 * 3 + FMT_E5M2: return launch_mb<A_BF16, FMT_E5M2>(p, MB, S, mchunks, smem, stream);
-    case A_S8 * 3 + FMT_E4M3_REF: return launch_mb<A_S8, FMT_E4M3_REF>(p, MB, S, mchunks, smem, stream);
-    case A_S8 * 3 + FMT_E5M2: return launch_mb<A_S8, FMT_E5M2>(p, MB, S, mchunks, smem, stream);
+    case A_F16 * 3 + FMT_E4M3_REF: return launch_mb<A_F16, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_F16 * 3 + FMT_E5M2: return launch_mb<A_F16, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_BF16 * 3 + FMT_E4M3_REF: return launch_mb<A_BF16, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_BF16 * 3 + FMT_E5M2: return launch_mb<A_BF16, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_S8 * 3 + FMT_E4M3_REF: return launch_mb<A_S8, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_S8 * 3 + FMT_E5M2: return launch_mb<A_S8, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
     default: return cudaErrorInvalidValue;
   }
+}
+
+unsigned int gemv_device_error(bool clear) {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_fp8imma_device_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+  if (clear && v) {
+    unsigned int z = 0;
+    cudaMemcpyToSymbol(g_fp8imma_device_error, &z, sizeof(z));
+  }
+  return v;
 }
 
 }  // namespace fp8imma_b200

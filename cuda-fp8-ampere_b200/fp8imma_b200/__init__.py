@@ -40,6 +40,8 @@ EXT_SYMBOLS = [
     "fp8imma_set_splitk",
     "fp8imma_set_small_m_max",
     "fp8imma_last_path",
+    "fp8imma_set_pdl",
+    "fp8imma_device_error",
     "fp8imma_version",
 ]
 
@@ -84,6 +86,10 @@ def lib() -> ctypes.CDLL:
     L.fp8imma_set_splitk.argtypes = [I]
     L.fp8imma_set_small_m_max.restype = I
     L.fp8imma_set_small_m_max.argtypes = [I]
+    L.fp8imma_set_pdl.restype = I
+    L.fp8imma_set_pdl.argtypes = [I]
+    L.fp8imma_device_error.restype = ctypes.c_uint
+    L.fp8imma_device_error.argtypes = [I]
     L.fp8imma_last_path.restype = I
     L.fp8imma_last_path.argtypes = []
     L.fp8imma_version.restype = ctypes.c_char_p

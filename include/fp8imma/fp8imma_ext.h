@@ -73,10 +73,20 @@ int fp8imma_fp8wgt_linear_forward(const void* A_f16, const void* B_u8, float sca
 int fp8imma_set_splitk(int splits);
 // Largest M routed to the small-M split-K kernel (default 64).
 int fp8imma_set_small_m_max(int m);
+// Programmatic dependent launch (default off). When on, a GEMM may start
+// streaming its weights and reading its column scales while the previous
+// kernel in the stream is still running; activations are read, and outputs
+// written, only after that kernel has finished. Enable it only when weights
+// and scales are not written by the kernel launched just before the GEMM.
+int fp8imma_set_pdl(int enable);
 // Kernel family the last fp8imma call on this thread launched:
 // 0 none, 1 small-M split-K, 2 generic fallback, 3 tcgen05 GEMM, 4 native FP8.
 int fp8imma_last_path(void);
 const char* fp8imma_version(void);
+// Error word of the current device: non-zero when a kernel gave up a bounded
+// wait on its internal pipeline (the kernel then returned early and its output
+// is not valid). Synchronises the device. clear != 0 resets it.
+unsigned int fp8imma_device_error(int clear);
 
 #ifdef __cplusplus
 }  // extern "C"
