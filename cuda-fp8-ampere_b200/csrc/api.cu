@@ -63,6 +63,15 @@ static cudaError_t run_int8(GemvParams p, int a_type, int fmt, int group, cudaSt
   p.keff_a = p.K - p.K % group;
   p.pdl = g_pdl.load();
   const bool fast_shape = p.K > 0 && (p.K % 16) == 0 && aligned16(p.A) && aligned16(p.B);
+  if (fast_shape && p.M > g_small_m_max.load()) {
+    void* scratch = nullptr;
+    cudaError_t e = cudaMallocAsync(&scratch, gemm_tc_scratch_bytes(p.M, p.N, p.K, false), stream);
+    if (e != cudaSuccess) return e;
+    t_last_path = 3;
+    e = launch_gemm_tc_s8(p, a_type, fmt, scratch, stream);
+    cudaError_t e2 = cudaFreeAsync(scratch, stream);
+    return e != cudaSuccess ? e : e2;
+  }
   if (fast_shape) {
     t_last_path = 1;
     return launch_gemv_s8(p, a_type, fmt, g_splitk.load(), stream);
@@ -98,10 +107,31 @@ static int ref_launch(int kChunk, int a_type, int group, const void* A, const vo
 
 // ------------------------------------------------------- extended GEMM ----
 
+// Native FP8 path: activations quantised per row to E4M3, weights used as raw
+// E4M3FN / E5M2 bytes, fp32 accumulation, D = acc * row_scale * col_scale.
+static cudaError_t gemm_native(const fp8imma_gemm_args* a, cudaStream_t stream) {
+  if (a->M <= 0 || a->N <= 0) return cudaErrorInvalidConfiguration;
+  if (a->K <= 0 || !a->A || !a->B || !a->D || !a->col_scales_f32) return cudaErrorInvalidValue;
+  if (a->a_type != FP8IMMA_A_F16 && a->a_type != FP8IMMA_A_BF16) return cudaErrorInvalidValue;
+  if (a->b_format < 0 || a->b_format > 1 || a->out_type < 0 || a->out_type > 1 || a->out_layout < 0 ||
+      a->out_layout > 1)
+    return cudaErrorInvalidValue;
+  if ((a->K % 16) != 0 || !aligned16(a->A) || !aligned16(a->B)) return cudaErrorInvalidValue;
+  void* scratch = nullptr;
+  cudaError_t e = cudaMallocAsync(&scratch, gemm_tc_scratch_bytes(a->M, a->N, a->K, true), stream);
+  if (e != cudaSuccess) return e;
+  t_last_path = 4;
+  e = launch_gemm_tc_fp8(a->A, a->a_type, static_cast<const uint8_t*>(a->B), a->b_format, a->col_scales_f32, a->D,
+                         a->M, a->N, a->K, a->out_type, a->out_layout, scratch, stream);
+  cudaError_t e2 = cudaFreeAsync(scratch, stream);
+  return e != cudaSuccess ? e : e2;
+}
+
 static cudaError_t gemm_ex(const fp8imma_gemm_args* a, cudaStream_t stream) {
   t_last_path = 0;
   if (!a) return cudaErrorInvalidValue;
-  if (a->path != FP8IMMA_PATH_INT8_EXACT) return cudaErrorNotSupported;
+  if (a->path == FP8IMMA_PATH_FP8_NATIVE) return gemm_native(a, stream);
+  if (a->path != FP8IMMA_PATH_INT8_EXACT) return cudaErrorInvalidValue;
   if (a->a_type < 0 || a->a_type > 2 || a->b_format < 0 || a->b_format > 1) return cudaErrorInvalidValue;
   if (a->out_type < 0 || a->out_type > 1 || a->out_layout < 0 || a->out_layout > 1) return cudaErrorInvalidValue;
   if (a->act_quant < 0 || a->act_quant > 1) return cudaErrorInvalidValue;
@@ -261,7 +291,7 @@ int fp8imma_set_pdl(int enable) {
   return 0;
 }
 
-unsigned int fp8imma_device_error(int clear) { return gemv_device_error(clear != 0); }
+unsigned int fp8imma_device_error(int clear) { return gemv_device_error(clear != 0) | tc_device_error(clear != 0); }
 
 const char* fp8imma_version(void) { return "fp8imma-b200 0.1 (sm_100a)"; }
 

@@ -49,6 +49,15 @@ int num_sms_current();
 cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaStream_t stream);
 int gemv_pick_splits(int N, int K, int mchunks, int num_sms);
 
+// Large-M tensor-core path (tcgen05). Scratch must hold
+// gemm_tc_scratch_bytes() bytes (16-byte aligned).
+size_t gemm_tc_scratch_bytes(int M, int N, int K, bool native);
+cudaError_t launch_gemm_tc_s8(const GemvParams& p, int a_type, int fmt, void* scratch, cudaStream_t stream);
+cudaError_t launch_gemm_tc_fp8(const void* A, int a_type, const uint8_t* B, int b_fmt, const float* col_scale,
+                               void* D, int M, int N, int K, int out_bf16, int out_row_major, void* scratch,
+                               cudaStream_t stream);
+unsigned int tc_device_error(bool clear);
+
 // Exact fallback for shapes the fast kernels do not take (any K, any alignment).
 cudaError_t launch_generic_s8(const GemvParams& p, int a_type, int fmt, cudaStream_t stream);
 

@@ -1,0 +1,560 @@
+// Large-M GEMM on the 5th-generation tensor cores (tcgen05, TMEM), sm_100a.
+//
+// Two paths share one persistent, warp-specialised kernel:
+//   * int8-exact (kind::i8, s32 accumulators in TMEM): activations and
+//     weights are first turned into int8 by two HBM-streaming prep kernels
+//     using exactly the reference rounding chain (fp8imma_device.cuh), then
+//     contracted. The int32 sums are exact, so the result equals the
+//     reference (src/fp8imma/impl/v4_kernels.inl) bit for bit.
+//   * native FP8 (kind::f8f6f4, f32 accumulators): weights are the raw
+//     E4M3/E5M2 bytes (no transcode), activations are quantised per row to
+//     E4M3 by the prep kernel.
+// The GEMM computes D^T = W * X^T: the MMA's M side is 128 weight columns
+// (TMEM lanes), its N side 256 activation rows (TMEM columns), so each
+// epilogue thread owns one output column n and writes a contiguous run of
+// D[n*M + m] (the reference's col-major output).
+//
+// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
+// issuer, warps 2-5 epilogue. 4-stage smem ring of {16 KB weights, 32 KB
+// activations} (128-byte swizzle, K-major UMMA descriptors), two 256-column
+// TMEM accumulators so the epilogue of one tile overlaps the MMAs of the next.
+// All waits are bounded (sm100_async.cuh).
+#include "fp8imma_device.cuh"
+#include "fp8imma_kernels.h"
+#include "sm100_async.cuh"
+
+using namespace fp8imma_dev;
+
+namespace fp8imma_b200 {
+
+namespace {
+
+constexpr int kTileW = 128;  // weight columns per tile (MMA M)
+constexpr int kTileX = 256;  // activation rows per tile (MMA N)
+constexpr int kBK = 128;     // K bytes per stage
+constexpr int kStages = 4;
+constexpr int kBytesW = kTileW * kBK;
+constexpr int kBytesX = kTileX * kBK;
+constexpr int kStageBytes = kBytesW + kBytesX;
+constexpr int kThreadsTC = 192;
+constexpr int kTmemCols = 512;
+
+enum { KIND_I8 = 0, KIND_F8 = 1 };
+
+// ---------------------------------------------------------------- tcgen05 --
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+template <int KIND>
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  if (KIND == KIND_I8) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+  }
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 columns of 32-bit accumulators -> 32 registers per thread
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// UMMA shared-memory descriptor: K-major operand, 128-byte swizzle, rows of
+// 128 bytes, 8-row core groups 1024 bytes apart (SBO), sm_100 version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;                 // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;       // SBO
+  d |= (uint64_t)1 << 46;                 // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: M=128, N=256, K-major A and B.
+template <int KIND>
+__host__ __device__ constexpr uint32_t make_idesc(int a_fmt) {
+  // c_format [4,6): 1 = F32, 2 = S32; a_format [7,10); b_format [10,13);
+  // n_dim [17,23) = N>>3; m_dim [24,29) = M>>4
+  return (KIND == KIND_I8 ? (2u << 4) | (1u << 7) | (1u << 10) : (1u << 4) | ((uint32_t)a_fmt << 7) | (0u << 10)) |
+         ((uint32_t)(kTileX >> 3) << 17) | ((uint32_t)(kTileW >> 4) << 24);
+}
+
+struct TcParams {
+  int M, N, K;
+  int tiles_w, tiles_x;
+  uint32_t idesc;
+  const uint16_t* scale_u16;       // int8 path: reference column scales (fp16 bits)
+  unsigned long long scale_tex;    // or a texture over them
+  const float* col_scale_f32;      // optional fp32 column multiplier (native path: weight scale)
+  const float* row_g;              // per-row global scale (row quant / native row scale) or null
+  float global_scale;
+  void* D;
+  int32_t* acc_out;
+  int out_bf16, out_row_major;
+};
+
+template <int KIND>
+__global__ void __launch_bounds__(kThreadsTC, 1)
+    gemm_tc_kernel(const __grid_constant__ TcParams p, const __grid_constant__ CUtensorMap mapW,
+                   const __grid_constant__ CUtensorMap mapX) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntiles = p.tiles_w * p.tiles_x;
+  const int nkb = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tensormap(&mapW);
+      prefetch_tensormap(&mapX);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const int tw = tile % p.tiles_w, tx = tile / p.tiles_w;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY))) break;
+          uint8_t* sw = smem + stage * kStageBytes;
+          mbar_arrive_expect_tx(&full[stage], kStageBytes);
+          tma_load_2d(sw, &mapW, &full[stage], kb * kBK, tw * kTileW);
+          tma_load_2d(sw + kBytesW, &mapX, &full[stage], kb * kBK, tx * kTileX);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // drain: every load issued must have landed before the CTA may exit
+      for (int s = 0; s < kStages && ok; ++s) {
+        // the last use of each stage is observed by the MMA issuer; waiting on
+        // its release here guarantees the bytes arrived and were consumed
+        ok = mbar_wait(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+        const int buf = it & 1;
+        if (!(ok = mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1u, ERR_WAIT_TMEM_EMPTY))) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * kTileX);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!(ok = mbar_wait(&full[stage], phase, ERR_WAIT_FULL))) break;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+          const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + kBytesW);
+#pragma unroll
+          for (int j = 0; j < kBK / 32; ++j)
+            umma<KIND>(d_tmem, adesc + 2 * j, bdesc + 2 * j, p.idesc, (kb | j) != 0);
+          umma_commit(&empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        umma_commit(&tfull[buf]);
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, ERR_WAIT_FULL);
+    }
+  } else {
+    // ------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int it = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+      const int buf = it & 1;
+      const int tw = tile % p.tiles_w, tx = tile / p.tiles_w;
+      if (!mbar_wait(&tfull[buf], (it >> 1) & 1, ERR_WAIT_TMEM_FULL)) break;
+      tc_fence_after();
+      const int n = tw * kTileW + q * 32 + lane;
+      const bool nok = n < p.N;
+      float cs = 1.0f;
+      if (nok) {
+        if (KIND == KIND_I8) {
+          uint16_t sb = p.scale_tex ? tex1Dfetch<unsigned short>((cudaTextureObject_t)p.scale_tex, n) : p.scale_u16[n];
+          cs = __half2float(__ushort_as_half(sb));
+        }
+      }
+      const float cs2 = (nok && p.col_scale_f32) ? p.col_scale_f32[n] : 1.0f;
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kTileX);
+      uint16_t* D = static_cast<uint16_t*>(p.D);
+#pragma unroll 1
+      for (int j0 = 0; j0 < kTileX; j0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + j0, r);
+        const int mbase = tx * kTileX + j0;
+        if (!nok || mbase >= p.M) continue;
+        uint16_t o[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int m = mbase + j;
+          float v;
+          if (KIND == KIND_I8) {
+            float se = cs * (p.row_g ? p.row_g[m < p.M ? m : 0] : p.global_scale);
+            if (p.col_scale_f32) se = se * cs2;
+            v = (float)(int32_t)r[j] * se;
+          } else {
+            float rs = p.row_g ? p.row_g[m < p.M ? m : 0] : 1.0f;
+            v = __uint_as_float(r[j]) * rs * cs2;
+          }
+          o[j] = store_val(v, p.out_bf16);
+        }
+        const int mcount = min(32, p.M - mbase);
+        if (p.out_row_major) {
+          for (int j = 0; j < mcount; ++j) D[(size_t)(mbase + j) * p.N + n] = o[j];
+        } else {
+          uint16_t* dst = D + (size_t)n * p.M + mbase;
+          if (mcount == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
+#pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4) {
+              uint4 w;
+              w.x = (uint32_t)o[8 * v4 + 0] | ((uint32_t)o[8 * v4 + 1] << 16);
+              w.y = (uint32_t)o[8 * v4 + 2] | ((uint32_t)o[8 * v4 + 3] << 16);
+              w.z = (uint32_t)o[8 * v4 + 4] | ((uint32_t)o[8 * v4 + 5] << 16);
+              w.w = (uint32_t)o[8 * v4 + 6] | ((uint32_t)o[8 * v4 + 7] << 16);
+              reinterpret_cast<uint4*>(dst)[v4] = w;
+            }
+          } else {
+            for (int j = 0; j < mcount; ++j) dst[j] = o[j];
+          }
+        }
+        if (KIND == KIND_I8 && p.acc_out) {
+          for (int j = 0; j < mcount; ++j) p.acc_out[(size_t)n * p.M + mbase + j] = (int32_t)r[j];
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------ prep kernels --
+
+// Activations -> int8 with the reference rounding (per-tensor or per-row
+// multiplier), 8 elements per thread-iteration. K % 8 == 0.
+template <int AT>
+__global__ void __launch_bounds__(256) quant_a_s8_kernel(const void* __restrict__ A, int M, int K, uint16_t a_inv_h,
+                                                         const uint16_t* __restrict__ row_inv_h, int8_t* __restrict__ Aq) {
+  const size_t total = (size_t)M * (K >> 3);
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = i << 3;
+    const int m = (int)(e / K);
+    uint2 out;
+    if (AT == A_S8) {
+      out = reinterpret_cast<const uint2*>(A)[i];
+    } else {
+      uint4 v = reinterpret_cast<const uint4*>(A)[i];
+      const uint16_t ainv = row_inv_h ? row_inv_h[m] : a_inv_h;
+      const uint32_t ainv2 = (uint32_t)ainv | ((uint32_t)ainv << 16);
+      if (AT == A_BF16) {
+        v.x = bf16x2_to_f16x2(v.x);
+        v.y = bf16x2_to_f16x2(v.y);
+        v.z = bf16x2_to_f16x2(v.z);
+        v.w = bf16x2_to_f16x2(v.w);
+      }
+      out.x = quant4_f16(v.x, v.y, ainv2);
+      out.y = quant4_f16(v.z, v.w, ainv2);
+    }
+    reinterpret_cast<uint2*>(Aq)[i] = out;
+  }
+}
+
+// FP8 weights -> int8 with the reference chain. One thread handles 64 bytes
+// of one weight row (amortising the per-column inverse scale). K % 16 == 0.
+template <int FMT>
+__global__ void __launch_bounds__(256) transcode_b_kernel(const uint8_t* __restrict__ B, int N, int K,
+                                                          const uint16_t* __restrict__ scale_u16,
+                                                          unsigned long long scale_tex, int8_t* __restrict__ Bq) {
+  const int chunks = (K + 63) >> 6;
+  const size_t total = (size_t)N * chunks;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int n = (int)(i / chunks);
+    const int k0 = (int)(i - (size_t)n * chunks) << 6;
+    const uint16_t sb = scale_tex ? tex1Dfetch<unsigned short>((cudaTextureObject_t)scale_tex, n) : scale_u16[n];
+    const uint16_t inv = inv_scale_bits(sb);
+    const bool fast = fast_ok<FMT>(inv);
+    const uint32_t fs = fast_scale<FMT>(inv);
+    const uint4* src = reinterpret_cast<const uint4*>(B + (size_t)n * K + k0);
+    uint4* dst = reinterpret_cast<uint4*>(Bq + (size_t)n * K + k0);
+    const int nv = min(4, (K - k0) >> 4);
+    uint4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < nv) v[j] = ldg_stream_v4(src + j);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j < nv) {
+        uint4 o;
+        if (fast) {
+          if (FMT == FMT_E5M2) {
+            o.x = transcode4_fast_e5m2(v[j].x, fs);
+            o.y = transcode4_fast_e5m2(v[j].y, fs);
+            o.z = transcode4_fast_e5m2(v[j].z, fs);
+            o.w = transcode4_fast_e5m2(v[j].w, fs);
+          } else {
+            o.x = transcode4_fast_e4m3(v[j].x, fs);
+            o.y = transcode4_fast_e4m3(v[j].y, fs);
+            o.z = transcode4_fast_e4m3(v[j].z, fs);
+            o.w = transcode4_fast_e4m3(v[j].w, fs);
+          }
+        } else {
+          o.x = transcode4_exact<FMT>(v[j].x, inv);
+          o.y = transcode4_exact<FMT>(v[j].y, inv);
+          o.z = transcode4_exact<FMT>(v[j].z, inv);
+          o.w = transcode4_exact<FMT>(v[j].w, inv);
+        }
+        dst[j] = o;
+      }
+    }
+  }
+}
+
+// Native path: per-row E4M3 quantisation. One CTA (256 threads) per row:
+// absmax over to_half(a), row scale s = absmax/448, a8 = e4m3_rn_satfinite(a *
+// (448/absmax)). K % 8 == 0.
+template <int AT>
+__global__ void __launch_bounds__(256) quant_a_e4m3_kernel(const void* __restrict__ A, int M, int K,
+                                                           uint8_t* __restrict__ Aq, float* __restrict__ row_scale) {
+  const int m = blockIdx.x;
+  if (m >= M) return;
+  const uint16_t* row = static_cast<const uint16_t*>(A) + (size_t)m * K;
+  __shared__ float red[8];
+  float amax = 0.0f;
+  for (int k = threadIdx.x * 8; k < K; k += 256 * 8) {
+    uint4 v = *reinterpret_cast<const uint4*>(row + k);
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t h2 = AT == A_BF16 ? bf16x2_to_f16x2(w[j]) : w[j];
+      float2 f = __half22float2(*reinterpret_cast<__half2*>(&h2));
+      amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) amax = fmaxf(amax, red[i]);
+  float qs = 0.0f, s = 0.0f;
+  if (amax > 0.0f && amax <= 3.402823466e38f) {
+    qs = __fdiv_rn(448.0f, amax);
+    s = __fdiv_rn(amax, 448.0f);
+  }
+  if (threadIdx.x == 0) row_scale[m] = s;
+  uint8_t* out = Aq + (size_t)m * K;
+  for (int k = threadIdx.x * 8; k < K; k += 256 * 8) {
+    uint4 v = *reinterpret_cast<const uint4*>(row + k);
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      uint32_t h0 = AT == A_BF16 ? bf16x2_to_f16x2(w[2 * j]) : w[2 * j];
+      uint32_t h1 = AT == A_BF16 ? bf16x2_to_f16x2(w[2 * j + 1]) : w[2 * j + 1];
+      float2 f0 = __half22float2(*reinterpret_cast<__half2*>(&h0));
+      float2 f1 = __half22float2(*reinterpret_cast<__half2*>(&h1));
+      uint16_t lo, hi;
+      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(__fmul_rn(f0.y, qs)), "f"(__fmul_rn(f0.x, qs)));
+      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(__fmul_rn(f1.y, qs)), "f"(__fmul_rn(f1.x, qs)));
+      o[j] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    *reinterpret_cast<uint2*>(out + k) = make_uint2(o[0], o[1]);
+  }
+}
+
+int grid_for(size_t work_items) {
+  const int sms = num_sms_current();
+  size_t blocks = (work_items + 255) / 256;
+  size_t cap = (size_t)sms * 8;
+  return (int)(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
+
+template <int KIND>
+cudaError_t launch_tc(const TcParams& p, const CUtensorMap& mw, const CUtensorMap& mx, cudaStream_t stream) {
+  auto kern = gemm_tc_kernel<KIND>;
+  const int smem = kStages * kStageBytes + 1024 + 256;
+  cudaError_t e = ensure_smem_attr((const void*)kern, smem);
+  if (e != cudaSuccess) return e;
+  const int ntiles = p.tiles_w * p.tiles_x;
+  const int grid = ntiles < num_sms_current() ? ntiles : num_sms_current();
+  kern<<<grid, kThreadsTC, smem, stream>>>(p, mw, mx);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+unsigned int tc_device_error(bool clear) {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_fp8imma_device_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+  if (clear && v) {
+    unsigned int z = 0;
+    cudaMemcpyToSymbol(g_fp8imma_device_error, &z, sizeof(z));
+  }
+  return v;
+}
+
+size_t gemm_tc_scratch_bytes(int M, int N, int K, bool native) {
+  size_t a = ((size_t)M * K + 255) & ~size_t(255);
+  size_t b = native ? 0 : (((size_t)N * K + 255) & ~size_t(255));
+  size_t r = native ? (((size_t)M * 4 + 255) & ~size_t(255)) : 0;
+  return a + b + r;
+}
+
+// int8-exact large-M GEMM: prep (A quant, B transcode) into `scratch`, then tcgen05.
+cudaError_t launch_gemm_tc_s8(const GemvParams& gp, int a_type, int fmt, void* scratch, cudaStream_t stream) {
+  const int M = gp.M, N = gp.N, K = gp.K;
+  int8_t* Aq = static_cast<int8_t*>(scratch);
+  int8_t* Bq = Aq + (((size_t)M * K + 255) & ~size_t(255));
+  // 1. activations
+  {
+    const size_t items = (size_t)M * (K >> 3);
+    const int grid = grid_for(items);
+    switch (a_type) {
+      case A_F16: quant_a_s8_kernel<A_F16><<<grid, 256, 0, stream>>>(gp.A, M, K, gp.a_inv_h, gp.row_inv_h, Aq); break;
+      case A_BF16: quant_a_s8_kernel<A_BF16><<<grid, 256, 0, stream>>>(gp.A, M, K, gp.a_inv_h, gp.row_inv_h, Aq); break;
+      default: quant_a_s8_kernel<A_S8><<<grid, 256, 0, stream>>>(gp.A, M, K, gp.a_inv_h, gp.row_inv_h, Aq); break;
+    }
+  }
+  // 2. weights
+  {
+    const size_t items = (size_t)N * ((K + 63) >> 6);
+    const int grid = grid_for(items);
+    if (fmt == FMT_E5M2)
+      transcode_b_kernel<FMT_E5M2><<<grid, 256, 0, stream>>>(gp.B, N, K, gp.scale_u16, gp.scale_tex, Bq);
+    else
+      transcode_b_kernel<FMT_E4M3_REF><<<grid, 256, 0, stream>>>(gp.B, N, K, gp.scale_u16, gp.scale_tex, Bq);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // 3. tensor-core GEMM
+  CUtensorMap mw, mx;
+  if ((e = make_tmap_2d_u8(&mw, Bq, K, N, K, kBK, kTileW, true)) != cudaSuccess) return e;
+  if ((e = make_tmap_2d_u8(&mx, Aq, K, M, K, kBK, kTileX, true)) != cudaSuccess) return e;
+  TcParams p = {};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.tiles_w = (N + kTileW - 1) / kTileW;
+  p.tiles_x = (M + kTileX - 1) / kTileX;
+  p.idesc = make_idesc<KIND_I8>(0);
+  p.scale_u16 = gp.scale_u16;
+  p.scale_tex = gp.scale_tex;
+  p.col_scale_f32 = gp.col_scale_f32;
+  p.row_g = gp.row_g;
+  p.global_scale = gp.global_scale;
+  p.D = gp.D;
+  p.acc_out = gp.acc_out;
+  p.out_bf16 = gp.out_bf16;
+  p.out_row_major = gp.out_row_major;
+  return launch_tc<KIND_I8>(p, mw, mx, stream);
+}
+
+// Native FP8 large-M GEMM: per-row E4M3 activation quant, then kind::f8f6f4
+// on the raw weight bytes. b_fmt: 0 = E4M3 (hardware E4M3FN), 1 = E5M2.
+cudaError_t launch_gemm_tc_fp8(const void* A, int a_type, const uint8_t* B, int b_fmt, const float* col_scale,
+                               void* D, int M, int N, int K, int out_bf16, int out_row_major, void* scratch,
+                               cudaStream_t stream) {
+  uint8_t* Aq = static_cast<uint8_t*>(scratch);
+  float* rs = reinterpret_cast<float*>(Aq + (((size_t)M * K + 255) & ~size_t(255)));
+  if (a_type == A_BF16) quant_a_e4m3_kernel<A_BF16><<<M, 256, 0, stream>>>(A, M, K, Aq, rs);
+  else quant_a_e4m3_kernel<A_F16><<<M, 256, 0, stream>>>(A, M, K, Aq, rs);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  CUtensorMap mw, mx;
+  if ((e = make_tmap_2d_u8(&mw, B, K, N, K, kBK, kTileW, true)) != cudaSuccess) return e;
+  if ((e = make_tmap_2d_u8(&mx, Aq, K, M, K, kBK, kTileX, true)) != cudaSuccess) return e;
+  TcParams p = {};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.tiles_w = (N + kTileW - 1) / kTileW;
+  p.tiles_x = (M + kTileX - 1) / kTileX;
+  p.idesc = make_idesc<KIND_F8>(b_fmt == 1 ? 1 : 0);
+  p.col_scale_f32 = col_scale;
+  p.row_g = rs;
+  p.global_scale = 1.0f;
+  p.D = D;
+  p.out_bf16 = out_bf16;
+  p.out_row_major = out_row_major;
+  return launch_tc<KIND_F8>(p, mw, mx, stream);
+}
+
+}  // namespace fp8imma_b200
