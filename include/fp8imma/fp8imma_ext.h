@@ -61,6 +61,27 @@ typedef struct fp8imma_gemm_args {
 // buffers (cudaMallocAsync on `stream`).
 int fp8imma_gemm(const fp8imma_gemm_args* args, void* stream);
 
+// Largest M accepted by fp8imma_gemm_rowquant_noalloc.
+#define FP8IMMA_NOALLOC_MAX_M 4096
+
+// Allocation-free per-row-quantised GEMM. No counterpart in the reference (it
+// has no per-row quantisation). Same arguments and results as fp8imma_gemm
+// with path = FP8IMMA_PATH_INT8_EXACT and act_quant = FP8IMMA_AQ_ROW, for
+// callers that may not allocate device memory: runtimes that reserve HBM for
+// their own pool up front, serving loops that forbid allocation on the
+// request path, and plugin hosts that pass the plugin only caller-owned
+// buffers. The caller still passes A, B, scales and D; the per-row values the
+// two internal kernels exchange live in a fixed device array of
+// FP8IMMA_NOALLOC_MAX_M rows (24 KB) that every GPU loading the library keeps
+// until exit. M > FP8IMMA_NOALLOC_MAX_M returns cudaErrorInvalidValue.
+// It calls no cudaMalloc / cudaFree / cudaMallocAsync. The first call on each
+// device looks up the array's device address (cudaGetSymbolAddress, with that
+// device current); make that first call before any stream capture. Every call
+// on a device shares the one array (each call overwrites the rows it uses
+// before reading them), so calls that overlap on the GPU, e.g. on two streams
+// at once, race and must not be issued.
+int fp8imma_gemm_rowquant_noalloc(const fp8imma_gemm_args* args, void* stream);
+
 // fp8wgt linear: C[M,N] (fp32, row-major) = A[M,K] (fp16) x decode(B[N,K])^T,
 // decode(b) = fp16_rn(float(lut_e4m3[b]) * scale_b). Replaces
 // torch_ext/fp8wgt/fp8wgt_ext_cuda.cu:223 fp8_linear_forward (kernel :135),
