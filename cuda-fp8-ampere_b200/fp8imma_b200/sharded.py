@@ -36,7 +36,7 @@ class ColumnParallelFP8Gemm:
     (col-major MxN) on every rank."""
 
     def __init__(self, B_local: torch.Tensor, scales_local: torch.Tensor, N_total: int,
-                 group=None, col_scales_f32: torch.Tensor | None = None):
+                 group=None, col_scales_f32: torch.Tensor | None = None, local_fn=None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -47,10 +47,16 @@ class ColumnParallelFP8Gemm:
         self.n_local = self.B.shape[0]
         if self.world > 1 and N_total % self.world != 0:
             raise ValueError("N_total must divide evenly across ranks for the gather")
-        self._ext = ext()
+        # local_fn(A, B, scales, col_scales_f32, global_scale, a_inv_scale, act_quant, out) -> D [n_local, M];
+        # the default is the sm_100a kernel through the torch extension
+        self._local_fn = local_fn
+        self._ext = None if local_fn is not None else ext()
 
     def local(self, A: torch.Tensor, out: torch.Tensor | None = None, global_scale: float = 1.0,
               a_inv_scale: float = 1.0, act_quant: str = "tensor") -> torch.Tensor:
+        if self._local_fn is not None:
+            return self._local_fn(A, self.B, self.scales, self.col_scales_f32, global_scale, a_inv_scale, act_quant,
+                                  out)
         D, _ = self._ext.imma_fp8_gemm(A, self.B, self.scales, self.col_scales_f32, global_scale, a_inv_scale,
                                        act_quant, "e4m3", "int8", "float16", "col", False, out)
         return D
@@ -64,5 +70,10 @@ class ColumnParallelFP8Gemm:
             return self.local(A, out_full, global_scale, a_inv_scale, act_quant)
         mine = out_full.narrow(0, self.rank * self.n_local, self.n_local)
         self.local(A, mine, global_scale, a_inv_scale, act_quant)
-        dist.all_gather_into_tensor(out_full, mine, group=self.group)
+        if dist.get_backend(self.group) == "nccl":
+            # in place: this rank's slice already sits at its offset of out_full
+            dist.all_gather_into_tensor(out_full, mine, group=self.group)
+        else:
+            parts = list(out_full.chunk(self.world, dim=0))
+            dist.all_gather(parts, mine.clone(), group=self.group)
         return out_full
