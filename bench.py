@@ -424,42 +424,56 @@ def time_reference_lib(A, Bs, s16, M, N, K, gs, ainv, steps, copies):
 
 
 def time_points(ext, steps):
+    """Other benchmark shapes, both paths: decode and 70B-style (split-K
+    kernels), prefill / square / 70B M=4096 (tcgen05). CUDA-graph timed,
+    weights rotated over > 2x L2 where they would fit in it."""
     import torch
 
     from fp8imma_b200 import workloads as WL
 
+    shapes = {"decode_m1": (1, 4096, 4096), "decode_m4": (4, 4096, 4096), "decode_m16": (16, 4096, 4096),
+              "up70b_m1": (1, 28672, 8192), "up70b_m32": (32, 28672, 8192), "prefill": (2048, 11008, 4096),
+              "square4096": (4096, 4096, 4096), "square8192": (8192, 8192, 8192), "up70b_m4096": (4096, 28672, 8192)}
     out = {}
-    for name in ("decode_m1", "decode_m4", "decode_m16", "up70b_m1", "up70b_m32"):
-        w = WORKLOADS[name]
-        M, N, K = w["M"], w["N"], w["K"]
-        B, s16, _ = WL.make_weights(N, K, w["sigma_w"], "e4m3", seed=0)
-        A = WL.make_activations(M, K, w["dist"], w.get("outlier_frac", 0.0), seed=1)
+    for name, (M, N, K) in shapes.items():
+        w = WL.CONFIGS.get(name, {})
+        B, s16, sig = WL.make_weights(N, K, w.get("sigma_w", 0.02), "e4m3", seed=0)
+        A = WL.make_activations(M, K, w.get("dist", "normal"), w.get("outlier_frac", 0.0), seed=1)
         l2 = torch.cuda.get_device_properties(A.device).L2_cache_size
-        copies = max(1, math.ceil(2 * l2 / B.numel())) + 1
+        copies = max(1, math.ceil(2 * l2 / B.numel())) + 1 if B.numel() < 2 * l2 else 1
         Bs = [B] + [B.clone() for _ in range(copies - 1)]
         D = torch.empty(N, M, dtype=torch.float16, device=A.device)
-        n = min(steps, 200)
-        for i in range(3):
-            ext.imma_fp8_gemm(A, Bs[i % copies], s16, None, 1.0, 8.0, "tensor", "e4m3", "int8", "float16", "col",
-                              False, D)
-        g = torch.cuda.CUDAGraph()
-        st = torch.cuda.Stream()
-        torch.cuda.synchronize()
-        with torch.cuda.graph(g, stream=st):
-            for i in range(n):
-                ext.imma_fp8_gemm(A, Bs[i % copies], s16, None, 1.0, 8.0, "tensor", "e4m3", "int8", "float16",
-                                  "col", False, D)
-        g.replay()
-        torch.cuda.synchronize()
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ev0.record()
-        g.replay()
-        ev1.record()
-        torch.cuda.synchronize()
-        ms = ev0.elapsed_time(ev1) / n
-        out[name] = {"us": round(ms * 1e3, 3), "GB/s": round(alg_bytes(M, N, K) / (ms * 1e-3) / 1e9, 1),
-                     "TFLOPS": round(2 * M * N * K / (ms * 1e-3) / 1e12, 3)}
-        del Bs, g
+        n = min(steps, 200) if M <= 64 else 10
+        for path in ("int8", "fp8"):
+            def call(i):
+                if path == "int8":
+                    ext.imma_fp8_gemm(A, Bs[i % copies], s16, None, 1.0 / 16, 16.0, "tensor", "e4m3", "int8",
+                                      "float16", "col", False, D)
+                else:
+                    ext.imma_fp8_gemm(A, Bs[i % copies], None, sig, 1.0, 1.0, "row", "e4m3", "fp8", "float16", "col",
+                                      False, D)
+            for i in range(3):
+                call(i)
+            g = torch.cuda.CUDAGraph()
+            st = torch.cuda.Stream()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=st):
+                for i in range(n):
+                    call(i)
+            g.replay()
+            torch.cuda.synchronize()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            g.replay()
+            ev1.record()
+            torch.cuda.synchronize()
+            ms = ev0.elapsed_time(ev1) / n
+            out["%s_%s" % (name, path)] = {"us": round(ms * 1e3, 3),
+                                          "GB/s": round(alg_bytes(M, N, K) / (ms * 1e-3) / 1e9, 1),
+                                          "TFLOPS": round(2 * M * N * K / (ms * 1e-3) / 1e12, 3),
+                                          "kernel_path": ext.last_path()}
+            del g
+        del Bs, B, A
         torch.cuda.empty_cache()
     return out
 

@@ -120,9 +120,32 @@ static cudaError_t gemm_native(const fp8imma_gemm_args* a, cudaStream_t stream) 
   void* scratch = nullptr;
   cudaError_t e = cudaMallocAsync(&scratch, gemm_tc_scratch_bytes(a->M, a->N, a->K, true), stream);
   if (e != cudaSuccess) return e;
-  t_last_path = 4;
-  e = launch_gemm_tc_fp8(a->A, a->a_type, static_cast<const uint8_t*>(a->B), a->b_format, a->col_scales_f32, a->D,
-                         a->M, a->N, a->K, a->out_type, a->out_layout, scratch, stream);
+  if (a->M <= g_small_m_max.load()) {
+    // small M: per-row E4M3 activations, then the split-K kernel with FP8 tensor-core MMAs
+    uint8_t* Aq = static_cast<uint8_t*>(scratch);
+    float* rs = reinterpret_cast<float*>(Aq + (((size_t)a->M * a->K + 255) & ~size_t(255)));
+    e = launch_quant_a_e4m3(a->A, a->a_type, a->M, a->K, Aq, rs, stream);
+    if (e == cudaSuccess) {
+      GemvParams p = {};
+      p.A = Aq;
+      p.B = static_cast<const uint8_t*>(a->B);
+      p.D = a->D;
+      p.row_g = rs;
+      p.col_scale_f32 = a->col_scales_f32;
+      p.M = a->M;
+      p.N = a->N;
+      p.K = a->K;
+      p.keff_a = a->K;
+      p.out_bf16 = a->out_type;
+      p.out_row_major = a->out_layout;
+      t_last_path = 5;
+      e = launch_gemv_s8(p, A_S8, a->b_format == FP8IMMA_B_E5M2 ? 3 : 2, g_splitk.load(), stream);
+    }
+  } else {
+    t_last_path = 4;
+    e = launch_gemm_tc_fp8(a->A, a->a_type, static_cast<const uint8_t*>(a->B), a->b_format, a->col_scales_f32,
+                           a->D, a->M, a->N, a->K, a->out_type, a->out_layout, scratch, stream);
+  }
   cudaError_t e2 = cudaFreeAsync(scratch, stream);
   return e != cudaSuccess ? e : e2;
 }

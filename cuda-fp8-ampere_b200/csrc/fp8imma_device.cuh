@@ -111,7 +111,9 @@ __device__ __forceinline__ uint16_t inv_scale_bits(uint16_t scale_bits) {
 
 // --------------------------------------------- weight transcode, 4 bytes --
 
-enum { FMT_E4M3_REF = 0, FMT_E5M2 = 1, FMT_E4M3FN = 2 };
+// int8-exact formats (transcoded): FMT_E4M3_REF, FMT_E5M2; native FP8 formats
+// (fed to the tensor core as bytes): FMT_E4M3FN, FMT_NATIVE_E5M2.
+enum { FMT_E4M3_REF = 0, FMT_E5M2 = 1, FMT_E4M3FN = 2, FMT_NATIVE_E5M2 = 3 };
 
 // Exact scalar path (any inverse scale): the reference chain byte by byte.
 template <int FMT>

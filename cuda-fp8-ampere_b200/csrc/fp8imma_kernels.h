@@ -57,6 +57,8 @@ cudaError_t launch_gemm_tc_fp8(const void* A, int a_type, const uint8_t* B, int 
                                void* D, int M, int N, int K, int out_bf16, int out_row_major, void* scratch,
                                cudaStream_t stream);
 unsigned int tc_device_error(bool clear);
+cudaError_t launch_quant_a_e4m3(const void* A, int a_type, int M, int K, uint8_t* Aq, float* row_scale,
+                                cudaStream_t stream);
 
 // Exact fallback for shapes the fast kernels do not take (any K, any alignment).
 cudaError_t launch_generic_s8(const GemvParams& p, int a_type, int fmt, cudaStream_t stream);

@@ -527,6 +527,14 @@ cudaError_t launch_gemm_tc_s8(const GemvParams& gp, int a_type, int fmt, void* s
   return launch_tc<KIND_I8>(p, mw, mx, stream);
 }
 
+// Per-row E4M3 activation quantisation alone (small-M native path).
+cudaError_t launch_quant_a_e4m3(const void* A, int a_type, int M, int K, uint8_t* Aq, float* row_scale,
+                                cudaStream_t stream) {
+  if (a_type == A_BF16) quant_a_e4m3_kernel<A_BF16><<<M, 256, 0, stream>>>(A, M, K, Aq, row_scale);
+  else quant_a_e4m3_kernel<A_F16><<<M, 256, 0, stream>>>(A, M, K, Aq, row_scale);
+  return cudaGetLastError();
+}
+
 // Native FP8 large-M GEMM: per-row E4M3 activation quant, then kind::f8f6f4
 // on the raw weight bytes. b_fmt: 0 = E4M3 (hardware E4M3FN), 1 = E5M2.
 cudaError_t launch_gemm_tc_fp8(const void* A, int a_type, const uint8_t* B, int b_fmt, const float* col_scale,

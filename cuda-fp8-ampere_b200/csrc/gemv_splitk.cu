@@ -54,6 +54,28 @@ __device__ __forceinline__ void mma_s8_16832(int (&c)[4], uint32_t a0, uint32_t 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// native FP8: weights (A operand) E4M3 or E5M2, activations E4M3, f32 accumulate
+template <int FMT>
+__device__ __forceinline__ void mma_f8_16832(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+  if (FMT == FMT_NATIVE_E5M2) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.f32.e5m2.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
+template <int FMT>
+constexpr bool is_native() { return FMT == FMT_E4M3FN || FMT == FMT_NATIVE_E5M2; }
+
 __device__ __forceinline__ uint4 lds128(const void* p) {
   uint4 r;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -69,6 +91,7 @@ __device__ __forceinline__ uint16_t load_col_scale_bits(const GemvParams& p, int
 
 template <int FMT, bool FAST>
 __device__ __forceinline__ uint32_t tc4(uint32_t x, uint32_t fscale, uint16_t inv_h) {
+  if (is_native<FMT>()) return x;  // FP8 bytes go to the tensor core as they are
   if (FAST) return FMT == FMT_E5M2 ? transcode4_fast_e5m2(x, fscale) : transcode4_fast_e4m3(x, fscale);
   return transcode4_exact<FMT>(x, inv_h);
 }
@@ -144,8 +167,14 @@ __device__ __forceinline__ void consumer_loop(const GemvParams& p, int (&acc)[MB
 #pragma unroll
       for (int nb = 0; nb < MB; ++nb) {
         uint4 q = lds128(arow + (nb * 8 + g) * astride);
-        mma_s8_16832(acc[nb], wa0, wb0, wa1, wb1, q.x, q.y);
-        mma_s8_16832(acc[nb], wa2, wb2, wa3, wb3, q.z, q.w);
+        if (is_native<FMT>()) {
+          float(&fa)[4] = *reinterpret_cast<float(*)[4]>(&acc[nb][0]);
+          mma_f8_16832<FMT>(fa, wa0, wb0, wa1, wb1, q.x, q.y);
+          mma_f8_16832<FMT>(fa, wa2, wb2, wa3, wb3, q.z, q.w);
+        } else {
+          mma_s8_16832(acc[nb], wa0, wb0, wa1, wb1, q.x, q.y);
+          mma_s8_16832(acc[nb], wa2, wb2, wa3, wb3, q.z, q.w);
+        }
       }
     }
     __syncwarp();
@@ -214,8 +243,8 @@ __global__ void __launch_bounds__(kThreads, 3)
   } else {
     const int col0 = tile_n0 + lc0, col1 = col0 + 8;
     const bool ok0 = col0 < p.N, ok1 = col1 < p.N;
-    const uint16_t inv0 = ok0 ? inv_scale_bits(load_col_scale_bits(p, col0)) : (uint16_t)0x3C00u;
-    const uint16_t inv1 = ok1 ? inv_scale_bits(load_col_scale_bits(p, col1)) : (uint16_t)0x3C00u;
+    const uint16_t inv0 = (ok0 && !is_native<FMT>()) ? inv_scale_bits(load_col_scale_bits(p, col0)) : (uint16_t)0x3C00u;
+    const uint16_t inv1 = (ok1 && !is_native<FMT>()) ? inv_scale_bits(load_col_scale_bits(p, col1)) : (uint16_t)0x3C00u;
     const bool all_fast = named_bar_and(2, kConsumers, fast_ok<FMT>(inv0) && fast_ok<FMT>(inv1));
     if (p.pdl) pdl_wait();  // activations may come from the previous kernel
     const uint32_t fs0 = fast_scale<FMT>(inv0), fs1 = fast_scale<FMT>(inv1);
@@ -256,6 +285,21 @@ __global__ void __launch_bounds__(kThreads, 3)
       mr = e % MR;
     }
     int n = tile_n0 + lc, m = m0 + mr;
+    if (is_native<FMT>()) {
+      float fs = 0.0f;
+      for (int q = 0; q < S; ++q) {
+        const int32_t* rp = cluster.map_shared_rank(part, q);
+        fs += __int_as_float(rp[lc * MR + mr]);
+      }
+      if (n < p.N && m < p.M) {
+        float v = fs * p.row_g[m] * (p.col_scale_f32 ? p.col_scale_f32[n] : 1.0f);
+        uint16_t o = store_val(v, p.out_bf16);
+        uint16_t* D = static_cast<uint16_t*>(p.D);
+        if (p.out_row_major) D[(size_t)m * p.N + n] = o;
+        else D[(size_t)n * p.M + m] = o;
+      }
+      continue;
+    }
     int32_t s = 0;
     for (int q = 0; q < S; ++q) {
       const int32_t* rp = cluster.map_shared_rank(part, q);
@@ -319,6 +363,7 @@ int gemv_pick_splits(int N, int K, int mchunks, int num_sms) {
 }
 
 cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaStream_t stream) {
+  if (fmt == FMT_E4M3FN || fmt == FMT_NATIVE_E5M2) a_type = A_S8;  // pre-quantised E4M3 activations are copied
   const int MB = p.M >= 32 ? 4 : (p.M + 7) / 8;
   const int MR = MB * 8;
   const int mchunks = (p.M + MR - 1) / MR;
@@ -336,13 +381,15 @@ cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaSt
   cudaError_t e = make_tmap_2d_u8(&tmap, p.B, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)p.K, kBlockK, kTileN,
                                   /*swizzle128=*/true);
   if (e != cudaSuccess) return e;
-  switch (a_type * 3 + fmt) {
-    case A_F16 * 3 + FMT_E4M3_REF: return launch_mb<A_F16, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_F16 * 3 + FMT_E5M2: return launch_mb<A_F16, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_BF16 * 3 + FMT_E4M3_REF: return launch_mb<A_BF16, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_BF16 * 3 + FMT_E5M2: return launch_mb<A_BF16, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_S8 * 3 + FMT_E4M3_REF: return launch_mb<A_S8, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_S8 * 3 + FMT_E5M2: return launch_mb<A_S8, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
+  switch (a_type * 4 + fmt) {
+    case A_F16 * 4 + FMT_E4M3_REF: return launch_mb<A_F16, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_F16 * 4 + FMT_E5M2: return launch_mb<A_F16, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_BF16 * 4 + FMT_E4M3_REF: return launch_mb<A_BF16, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_BF16 * 4 + FMT_E5M2: return launch_mb<A_BF16, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_S8 * 4 + FMT_E4M3_REF: return launch_mb<A_S8, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_S8 * 4 + FMT_E5M2: return launch_mb<A_S8, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_S8 * 4 + FMT_E4M3FN: return launch_mb<A_S8, FMT_E4M3FN>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_S8 * 4 + FMT_NATIVE_E5M2: return launch_mb<A_S8, FMT_NATIVE_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -101,7 +101,8 @@ int fp8imma_set_small_m_max(int m);
 // and scales are not written by the kernel launched just before the GEMM.
 int fp8imma_set_pdl(int enable);
 // Kernel family the last fp8imma call on this thread launched:
-// 0 none, 1 small-M split-K, 2 generic fallback, 3 tcgen05 GEMM, 4 native FP8.
+// 0 none, 1 small-M split-K, 2 generic fallback, 3 tcgen05 GEMM, 4 native FP8
+// tcgen05 GEMM, 5 native FP8 small-M split-K.
 int fp8imma_last_path(void);
 const char* fp8imma_version(void);
 // Error word of the current device: non-zero when a kernel gave up a bounded

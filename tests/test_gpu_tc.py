@@ -15,7 +15,7 @@ from helpers import cabi_ref_launch
 
 pytestmark = pytest.mark.gpu
 
-TC_PATH, GEMV_PATH, NATIVE_PATH = 3, 1, 4
+TC_PATH, GEMV_PATH, NATIVE_PATH, NATIVE_SK_PATH = 3, 1, 4, 5
 
 
 @pytest.mark.parametrize("variant", ["v4_f16", "v4_bf16", "v3_f16", "v2"])
@@ -100,7 +100,9 @@ def test_tc_full_size_square4096_row_slices_and_splitk_agreement(cuda):
 
 
 @pytest.mark.parametrize("M,N,K,fmt,a_bf16", [(256, 256, 512, "e4m3", False), (300, 200, 1024, "e5m2", False),
-                                               (1024, 512, 2048, "e4m3", True), (64, 384, 256, "e4m3", False)])
+                                               (1024, 512, 2048, "e4m3", True), (64, 384, 256, "e4m3", False),
+                                               (1, 4096, 4096, "e4m3", False), (16, 1000, 1024, "e5m2", True),
+                                               (33, 640, 512, "e4m3", False)])
 def test_native_fp8_matches_oracle(cuda, M, N, K, fmt, a_bf16):
     """Native FP8 path tolerance: fp16 outputs within 2e-3 relative (to the
     output's max magnitude) of the oracle, which uses the same quantised
@@ -113,7 +115,7 @@ def test_native_fp8_matches_oracle(cuda, M, N, K, fmt, a_bf16):
     dA = torch.from_numpy(A.view(np.int16)).cuda().view(torch.bfloat16 if a_bf16 else torch.float16)
     D, _ = e.imma_fp8_gemm(dA, torch.from_numpy(B).cuda(), None, torch.from_numpy(sig).cuda(), 1.0, 1.0, "row", fmt,
                            "fp8", "float16", "col", False, None)
-    assert e.last_path() == NATIVE_PATH
+    assert e.last_path() == (NATIVE_PATH if M > 64 else NATIVE_SK_PATH)
     torch.cuda.synchronize()
     got = D.cpu().float().numpy()
     ref = D_o.view(np.float16).astype(np.float32)
