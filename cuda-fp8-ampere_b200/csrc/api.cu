@@ -21,6 +21,9 @@ std::atomic<int> g_splitk{0};
 std::atomic<int> g_small_m_max{64};
 std::atomic<int> g_pdl{0};
 thread_local int t_last_path = 0;
+#ifdef FP8IMMA_TRACE
+unsigned long long* g_trace = nullptr;  // trace builds only
+#endif
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -62,6 +65,9 @@ static cudaError_t run_int8(GemvParams p, int a_type, int fmt, int group, cudaSt
   if (p.K < 0 || !p.A || !p.B || !p.D || (!p.scale_u16 && !p.scale_tex)) return cudaErrorInvalidValue;
   p.keff_a = p.K - p.K % group;
   p.pdl = g_pdl.load();
+#ifdef FP8IMMA_TRACE
+  p.trace = g_trace;
+#endif
   const bool fast_shape = p.K > 0 && (p.K % 16) == 0 && aligned16(p.A) && aligned16(p.B);
   if (fast_shape && p.M > g_small_m_max.load()) {
     void* scratch = nullptr;
@@ -245,6 +251,10 @@ cudaError_t launch_imma_fp8_actquant_v4_texscale_bf16(int kChunk, const __nv_bfl
 
 // --------------------------------------------------------------- C ABI -----
 extern "C" {
+
+#ifdef FP8IMMA_TRACE
+void fp8imma_debug_set_trace(void* buf) { g_trace = static_cast<unsigned long long*>(buf); }
+#endif
 
 void fp8imma_init_fp8_e4m3_lut(void) { fp8imma::init_fp8_e4m3_lut(); }
 

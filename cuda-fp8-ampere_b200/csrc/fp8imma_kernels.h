@@ -32,6 +32,7 @@ struct GemvParams {
   int out_bf16;
   int out_row_major;
   int pdl;                          // launched with programmatic stream serialisation
+  unsigned long long* trace;        // FP8IMMA_TRACE builds only: per-CTA phase timestamps
 };
 
 cudaError_t ensure_smem_attr(const void* kernel, int bytes);

@@ -28,6 +28,22 @@
 
 #include <cooperative_groups.h>
 
+// Opt-in phase tracing (compile with -DFP8IMMA_TRACE): thread 0 of each CTA
+// records %globaltimer at fixed points into p.trace[cta * 16 + point].
+#ifdef FP8IMMA_TRACE
+#define TRACE_POINT(p, i)                                                                                 \
+  do {                                                                                                     \
+    if ((p).trace && (threadIdx.x & 31) == 0) {                                                           \
+      unsigned long long t_;                                                                               \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                             \
+      const int cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);                    \
+      (p).trace[(size_t)cta_ * 16 + (i)] = t_;                                                             \
+    }                                                                                                      \
+  } while (0)
+#else
+#define TRACE_POINT(p, i) do { } while (0)
+#endif
+
 namespace cg = cooperative_groups;
 using namespace fp8imma_dev;
 
@@ -43,7 +59,10 @@ constexpr int kBlockK = 128;
 constexpr int kStages = 4;
 constexpr int kStageBytes = kTileN * kBlockK;
 constexpr int kBarOffset = kStages * kStageBytes;
-constexpr int kAqOffset = kBarOffset + 1024;
+constexpr int kScaleOffset = kBarOffset + 256;       // float[128] fp16 column scales
+constexpr int kColScaleOffset = kBarOffset + 768;    // float[128] fp32 column multipliers
+constexpr int kRowScaleOffset = kBarOffset + 1280;   // float[32] per-row / global scale
+constexpr int kAqOffset = kBarOffset + 2048;
 
 __device__ __forceinline__ void mma_s8_16832(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                              uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -74,7 +93,7 @@ __device__ __forceinline__ void mma_f8_16832(float (&c)[4], uint32_t a0, uint32_
 }
 
 template <int FMT>
-constexpr bool is_native() { return FMT == FMT_E4M3FN || FMT == FMT_NATIVE_E5M2; }
+__host__ __device__ constexpr bool is_native() { return FMT == FMT_E4M3FN || FMT == FMT_NATIVE_E5M2; }
 
 __device__ __forceinline__ uint4 lds128(const void* p) {
   uint4 r;
@@ -101,31 +120,52 @@ __device__ __forceinline__ uint32_t tc4(uint32_t x, uint32_t fscale, uint16_t in
 template <int AT, int MR>
 __device__ __forceinline__ void quant_chunk(const GemvParams& p, int8_t* aq, int stride, int m0, int k0, int len,
                                             int kvalid) {
+  constexpr int kBatch = 4;  // loads in flight per thread before any is converted
   const int items_per_row = len >> 3;  // 8 elements per item
   const int total = MR * items_per_row;
-  for (int it = threadIdx.x; it < total; it += kConsumers) {
-    int r = it / items_per_row;
-    int c = (it - r * items_per_row) << 3;
-    int m = m0 + r, k = k0 + c;
-    uint2 out = make_uint2(0u, 0u);
-    if (m < p.M && k < kvalid) {
-      if (AT == A_S8) {
-        out = *reinterpret_cast<const uint2*>(static_cast<const int8_t*>(p.A) + (size_t)m * p.K + k);
-      } else {
-        uint4 v = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.A) + (size_t)m * p.K + k);
-        uint16_t ainv = p.row_inv_h ? p.row_inv_h[m] : p.a_inv_h;
-        uint32_t ainv2 = (uint32_t)ainv | ((uint32_t)ainv << 16);
-        if (AT == A_BF16) {
-          v.x = bf16x2_to_f16x2(v.x);
-          v.y = bf16x2_to_f16x2(v.y);
-          v.z = bf16x2_to_f16x2(v.z);
-          v.w = bf16x2_to_f16x2(v.w);
-        }
-        out.x = quant4_f16(v.x, v.y, ainv2);
-        out.y = quant4_f16(v.z, v.w, ainv2);
+  for (int base = threadIdx.x; base < total; base += kBatch * kConsumers) {
+    uint4 v[kBatch];
+    bool live[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int it = base + j * kConsumers;
+      const int r = it / items_per_row, c = (it - r * items_per_row) << 3;
+      const int m = m0 + r, k = k0 + c;
+      live[j] = it < total && m < p.M && k < kvalid;
+      v[j] = make_uint4(0u, 0u, 0u, 0u);
+      if (live[j]) {
+        if (AT == A_S8)
+          *reinterpret_cast<uint2*>(&v[j]) =
+              *reinterpret_cast<const uint2*>(static_cast<const int8_t*>(p.A) + (size_t)m * p.K + k);
+        else
+          v[j] = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.A) + (size_t)m * p.K + k);
       }
     }
-    *reinterpret_cast<uint2*>(aq + r * stride + c) = out;
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int it = base + j * kConsumers;
+      if (it >= total) break;
+      const int r = it / items_per_row, c = (it - r * items_per_row) << 3;
+      uint2 out = make_uint2(0u, 0u);
+      if (live[j]) {
+        if (AT == A_S8) {
+          out = make_uint2(v[j].x, v[j].y);
+        } else {
+          const uint16_t ainv = p.row_inv_h ? p.row_inv_h[m0 + r] : p.a_inv_h;
+          const uint32_t ainv2 = (uint32_t)ainv | ((uint32_t)ainv << 16);
+          uint4 w = v[j];
+          if (AT == A_BF16) {
+            w.x = bf16x2_to_f16x2(w.x);
+            w.y = bf16x2_to_f16x2(w.y);
+            w.z = bf16x2_to_f16x2(w.z);
+            w.w = bf16x2_to_f16x2(w.w);
+          }
+          out.x = quant4_f16(w.x, w.y, ainv2);
+          out.y = quant4_f16(w.z, w.w, ainv2);
+        }
+      }
+      *reinterpret_cast<uint2*>(aq + r * stride + c) = out;
+    }
   }
 }
 
@@ -144,15 +184,17 @@ __device__ __forceinline__ void consumer_loop(const GemvParams& p, int (&acc)[MB
   bool ok = true;
   for (int i = 0; i < nkb; ++i) {
     const int koff = (i * kBlockK) % p.kc;
-    if (koff == 0) {
+    if (koff == 0 && i > 0) {
       named_bar_sync(1, kConsumers);
       int k0 = kbeg + i * kBlockK;
       int len = min(p.kc, kend - k0);
       len = (len + 63) & ~63;
       quant_chunk<AT, MR>(p, aq, astride, m0, k0, len, kend);
       named_bar_sync(1, kConsumers);
+      if (i == 0 && threadIdx.x == 0) TRACE_POINT(p, 3);
     }
     if (ok) ok = mbar_wait(&full[stage], phase, ERR_WAIT_FULL);
+    if (i == 0 && threadIdx.x == 0) TRACE_POINT(p, 4);
     const uint8_t* st = stages + stage * kStageBytes;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -206,6 +248,7 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int nkb = kend > kbeg ? (kend - kbeg + kBlockK - 1) / kBlockK : 0;
   const int astride = p.kc + 64;  // +64 B: conflict-free 16-byte fragment loads
 
+  if (threadIdx.x == 0) TRACE_POINT(p, 0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -214,7 +257,6 @@ __global__ void __launch_bounds__(kThreads, 3)
     fence_barrier_init();
   }
   __syncthreads();
-  if (p.pdl) pdl_launch_dependents();
 
   const int g = lane >> 2;
   const int lc0 = warp * 16 + (g >> 1) + 4 * (g & 1);  // MMA rows g / g+8 -> tile columns lc0 / lc0+8
@@ -226,6 +268,21 @@ __global__ void __launch_bounds__(kThreads, 3)
   if (!consumer) {
     // ---- TMA producer: weights are streamed from the first cycle (they do
     // not depend on the previous kernel in the stream)
+    if (lane != 0) {
+      // the other 31 lanes pull this CTA's first activation chunk and its
+      // column scales towards L2 while the consumers start up
+      const int esz = AT == A_S8 ? 1 : 2;
+      const int rows = min(MR, p.M - m0);
+      const int bytes = (min(kend, kbeg + p.kc) - kbeg) * esz;
+      const int lines_per_row = (bytes + 127) >> 7;
+      const char* abase = static_cast<const char*>(p.A) + ((size_t)m0 * p.K + kbeg) * esz;
+      for (int i = lane - 1; i < rows * lines_per_row; i += 31) {
+        const int r = i / lines_per_row, l = i - r * lines_per_row;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(abase + (size_t)r * p.K * esz + ((size_t)l << 7)));
+      }
+      if (!is_native<FMT>() && !p.scale_tex && lane <= 2)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(p.scale_u16 + tile_n0) + (lane - 1) * 128));
+    }
     if (lane == 0) {
       prefetch_tensormap(&tmap);
       int stage = 0;
@@ -243,10 +300,36 @@ __global__ void __launch_bounds__(kThreads, 3)
   } else {
     const int col0 = tile_n0 + lc0, col1 = col0 + 8;
     const bool ok0 = col0 < p.N, ok1 = col1 < p.N;
-    const uint16_t inv0 = (ok0 && !is_native<FMT>()) ? inv_scale_bits(load_col_scale_bits(p, col0)) : (uint16_t)0x3C00u;
-    const uint16_t inv1 = (ok1 && !is_native<FMT>()) ? inv_scale_bits(load_col_scale_bits(p, col1)) : (uint16_t)0x3C00u;
-    const bool all_fast = named_bar_and(2, kConsumers, fast_ok<FMT>(inv0) && fast_ok<FMT>(inv1));
+    // column scales are requested first; their latency overlaps the first
+    // activation chunk's loads below
+    const uint16_t sb0 = (ok0 && !is_native<FMT>()) ? load_col_scale_bits(p, col0) : (uint16_t)0;
+    const uint16_t sb1 = (ok1 && !is_native<FMT>()) ? load_col_scale_bits(p, col1) : (uint16_t)0;
+    const float cs0 = (ok0 && p.col_scale_f32) ? p.col_scale_f32[col0] : 1.0f;
+    const float cs1 = (ok1 && p.col_scale_f32) ? p.col_scale_f32[col1] : 1.0f;
     if (p.pdl) pdl_wait();  // activations may come from the previous kernel
+    float rg = 0.0f;
+    if (threadIdx.x < MR && m0 + (int)threadIdx.x < p.M) rg = p.row_g ? p.row_g[m0 + threadIdx.x] : p.global_scale;
+    if (nkb > 0) {
+      int len = min(p.kc, kend - kbeg);
+      len = (len + 63) & ~63;
+      quant_chunk<AT, MR>(p, aq, astride, m0, kbeg, len, kend);
+    }
+    // epilogue constants staged in shared memory (no global loads at the end)
+    float* sc_s = reinterpret_cast<float*>(smem + kScaleOffset);
+    float* cs_s = reinterpret_cast<float*>(smem + kColScaleOffset);
+    if ((lane & 3) == 0) {
+      sc_s[lc0] = __half2float(__ushort_as_half(sb0));
+      sc_s[lc0 + 8] = __half2float(__ushort_as_half(sb1));
+    } else if ((lane & 3) == 1) {
+      cs_s[lc0] = cs0;
+      cs_s[lc0 + 8] = cs1;
+    }
+    if (threadIdx.x < MR) reinterpret_cast<float*>(smem + kRowScaleOffset)[threadIdx.x] = rg;
+    const uint16_t inv0 = (ok0 && !is_native<FMT>()) ? inv_scale_bits(sb0) : (uint16_t)0x3C00u;
+    const uint16_t inv1 = (ok1 && !is_native<FMT>()) ? inv_scale_bits(sb1) : (uint16_t)0x3C00u;
+    // CTA-uniform transcode choice; also the barrier that publishes chunk 0
+    const bool all_fast = named_bar_and(2, kConsumers, fast_ok<FMT>(inv0) && fast_ok<FMT>(inv1));
+    if (threadIdx.x == 0) TRACE_POINT(p, 2);
     const uint32_t fs0 = fast_scale<FMT>(inv0), fs1 = fast_scale<FMT>(inv1);
     if (all_fast)
       consumer_loop<AT, MB, FMT, true>(p, acc, stages, full, empty, aq, astride, m0, kbeg, kend, nkb, fs0, fs1,
@@ -258,6 +341,7 @@ __global__ void __launch_bounds__(kThreads, 3)
 
   // ---- partials -> shared memory, [128 cols][MR] int32
   __syncthreads();
+  if (p.pdl) pdl_launch_dependents();  // the next grid's prologue overlaps this epilogue
   if (consumer) {
     const int t = lane & 3;
 #pragma unroll
@@ -267,7 +351,9 @@ __global__ void __launch_bounds__(kThreads, 3)
     }
   }
   cg::cluster_group cluster = cg::this_cluster();
+  if (threadIdx.x == 0) TRACE_POINT(p, 5);
   cluster.sync();
+  if (threadIdx.x == 0) TRACE_POINT(p, 6);
   if (p.pdl) pdl_wait();  // outputs may still be read by the previous kernel
 
   // ---- cluster reduction + epilogue: CTA rank r finishes 128/S columns
@@ -275,48 +361,61 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int rank = (int)cluster.block_rank();
   const int cols_per = kTileN / S;
   const int nelem = cols_per * MR;
-  for (int e = threadIdx.x; e < nelem; e += kThreads) {
-    int lc, mr;
-    if (p.out_row_major) {
-      mr = e / cols_per;
-      lc = rank * cols_per + (e - mr * cols_per);
-    } else {
-      lc = rank * cols_per + e / MR;
-      mr = e % MR;
-    }
-    int n = tile_n0 + lc, m = m0 + mr;
-    if (is_native<FMT>()) {
-      float fs = 0.0f;
-      for (int q = 0; q < S; ++q) {
-        const int32_t* rp = cluster.map_shared_rank(part, q);
-        fs += __int_as_float(rp[lc * MR + mr]);
+  const float* sc_s = reinterpret_cast<const float*>(smem + kScaleOffset);
+  const float* cs_s = reinterpret_cast<const float*>(smem + kColScaleOffset);
+  const float* rg_s = reinterpret_cast<const float*>(smem + kRowScaleOffset);
+  uint16_t* D = static_cast<uint16_t*>(p.D);
+  constexpr int kEpiBatch = 4;  // partial-sum reads in flight per thread
+  for (int base = threadIdx.x; base < nelem; base += kEpiBatch * kThreads) {
+    int32_t sum[kEpiBatch];
+    int lcs[kEpiBatch], mrs[kEpiBatch];
+#pragma unroll
+    for (int j = 0; j < kEpiBatch; ++j) {
+      const int e = base + j * kThreads;
+      int lc = 0, mr = 0;
+      if (p.out_row_major) {
+        mr = e / cols_per;
+        lc = rank * cols_per + (e - mr * cols_per);
+      } else {
+        lc = rank * cols_per + e / MR;
+        mr = e % MR;
       }
-      if (n < p.N && m < p.M) {
-        float v = fs * p.row_g[m] * (p.col_scale_f32 ? p.col_scale_f32[n] : 1.0f);
-        uint16_t o = store_val(v, p.out_bf16);
-        uint16_t* D = static_cast<uint16_t*>(p.D);
-        if (p.out_row_major) D[(size_t)m * p.N + n] = o;
-        else D[(size_t)n * p.M + m] = o;
+      lcs[j] = lc;
+      mrs[j] = mr;
+      int32_t acc_s = 0;
+      float acc_f = 0.0f;
+      if (e < nelem) {
+        for (int q = 0; q < S; ++q) {
+          const int32_t v = cluster.map_shared_rank(part, q)[lc * MR + mr];
+          if (is_native<FMT>()) acc_f += __int_as_float(v);
+          else acc_s += v;
+        }
       }
-      continue;
+      sum[j] = is_native<FMT>() ? __float_as_int(acc_f) : acc_s;
     }
-    int32_t s = 0;
-    for (int q = 0; q < S; ++q) {
-      const int32_t* rp = cluster.map_shared_rank(part, q);
-      s += rp[lc * MR + mr];
-    }
-    if (n < p.N && m < p.M) {
-      float sc = __half2float(__ushort_as_half(load_col_scale_bits(p, n)));
-      float se = sc * (p.row_g ? p.row_g[m] : p.global_scale);
-      if (p.col_scale_f32) se = se * p.col_scale_f32[n];
-      uint16_t o = store_val((float)s * se, p.out_bf16);
-      uint16_t* D = static_cast<uint16_t*>(p.D);
+#pragma unroll
+    for (int j = 0; j < kEpiBatch; ++j) {
+      const int e = base + j * kThreads;
+      const int lc = lcs[j], mr = mrs[j];
+      const int n = tile_n0 + lc, m = m0 + mr;
+      if (e >= nelem || n >= p.N || m >= p.M) continue;
+      float v;
+      if (is_native<FMT>()) {
+        v = __int_as_float(sum[j]) * rg_s[mr] * cs_s[lc];
+      } else {
+        float se = sc_s[lc] * rg_s[mr];
+        if (p.col_scale_f32) se = se * cs_s[lc];
+        v = (float)sum[j] * se;
+        if (p.acc_out) p.acc_out[(size_t)n * p.M + m] = sum[j];
+      }
+      const uint16_t o = store_val(v, p.out_bf16);
       if (p.out_row_major) D[(size_t)m * p.N + n] = o;
       else D[(size_t)n * p.M + m] = o;
-      if (p.acc_out) p.acc_out[(size_t)n * p.M + m] = s;
     }
   }
+  if (threadIdx.x == 0) TRACE_POINT(p, 7);
   cluster.sync();  // keep shared memory alive until every peer has read it
+  if (threadIdx.x == 0) TRACE_POINT(p, 8);
 }
 
 template <int AT, int MB, int FMT>
