@@ -42,7 +42,11 @@ WORKLOADS = {
     "decode_m4": dict(M=4, N=4096, K=4096, sigma_w=0.02, dist="normal", outlier_frac=0.01),
     "up70b_m1": dict(M=1, N=28672, K=8192, sigma_w=0.015, dist="normal", outlier_frac=0.0),
     "up70b_m32": dict(M=32, N=28672, K=8192, sigma_w=0.015, dist="normal", outlier_frac=0.0),
+    # tensor-bound shapes (tcgen05 path); value is reported in TFLOPS for these
+    "square4096": dict(M=4096, N=4096, K=4096, sigma_w=0.02, dist="uniform4", outlier_frac=0.0),
+    "prefill": dict(M=2048, N=11008, K=4096, sigma_w=0.02, dist="normal", outlier_frac=0.0),
 }
+LAUNCHES_PER_CALL = {1: 1, 2: 1, 3: 3, 4: 2, 5: 2}  # by kernel path (fp8imma_last_path)
 
 
 def alg_bytes(M, N, K):
@@ -342,7 +346,18 @@ def main():
     e2e_val = world * bytes_step_rank / (e2e_ms / args.steps * 1e-3) / 1e9
 
     hbm, bf16, peak_kind = load_peaks()
-    achieved = bytes_step_rank / (kern_ms * 1e-3) / 1e9
+    tensor_bound = M > 64
+    if tensor_bound:
+        achieved = 2.0 * M * Nl * K / (kern_ms * 1e-3) / 1e12
+        peak = 2.0 * bf16  # dense int8/FP8 = 2x dense bf16 (nominal ratio); bf16 measured
+        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4),
+                "peak_source": "2 x MEASURED_PEAKS.json bf16_tflops (%s); int8/FP8 dense = 2x bf16 nominal" % peak_kind}
+    else:
+        achieved = bytes_step_rank / (kern_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4),
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (%s)" % peak_kind}
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
@@ -361,7 +376,8 @@ def main():
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": round(tflops if tensor_bound else value, 2),
+            "unit": "TFLOPS" if tensor_bound else "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u8", "data": "synthetic",
             "config": {"workload": args.workload, "M": M, "N_per_gpu": Nl, "N_total": N_tot, "K": K,
@@ -371,14 +387,12 @@ def main():
                        "timing": "CUDA graph of K steps" if world == 1 else "eager, NCCL all-gather in step",
                        "pdl": bool(args.pdl)},
             "tflops": round(tflops, 4),
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm, "unit": "GB/s",
-                         "frac": round(achieved / hbm, 4), "traffic": traffic,
-                         "peak_source": "%s (MEASURED_PEAKS.json hbm_gbs)" % peak_kind if peak_kind == "measured"
-                         else "fallback 6650 GB/s"},
+            "roofline": dict(roof, traffic=traffic),
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": M * K * 2,
+            "e2e": {"value": round(e2e_val * (2.0 * M * Nl * K / bytes_step_rank * 1e-3
+                                                 if tensor_bound else 1.0), 2), "unit": "TFLOPS" if tensor_bound else "GB/s", "h2d_bytes_per_step": M * K * 2,
                     "d2h_bytes_per_step": Nl * M * 2},
-            "gpu_launches": args.steps, "kernel_path": path_id, "clocks": clocks,
+            "gpu_launches": args.steps * LAUNCHES_PER_CALL.get(path_id, 1), "kernel_path": path_id, "clocks": clocks,
             "device_error": int(F.lib().fp8imma_device_error(0)),
         }
         line.update(extra)
