@@ -319,6 +319,11 @@ int fp8imma_set_small_m_max(int m) {
 
 int fp8imma_last_path(void) { return t_last_path; }
 
+int fp8imma_set_tc_pair(int enable) {
+  tc_set_pair_mode(enable != 0);
+  return 0;
+}
+
 int fp8imma_set_pdl(int enable) {
   g_pdl.store(enable ? 1 : 0);
   return 0;

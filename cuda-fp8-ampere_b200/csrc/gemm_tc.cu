@@ -440,6 +440,289 @@ __global__ void __launch_bounds__(256) quant_a_e4m3_kernel(const void* __restric
   }
 }
 
+
+// ---------------------------------------------------------------- 2-SM ----
+// cta_group::2 variant: a cluster of two CTAs computes a 256 (weight columns)
+// x 256 (activation rows) tile with one M=256 MMA issued by the even CTA. Each
+// CTA stages half of both operands (128 weight rows, 128 activation rows per
+// 128-byte K step, 32 KB per stage, 6 stages), so every operand byte moved
+// through L2 and shared memory feeds twice the MACs of the 1-CTA kernel. Both
+// CTAs' TMA loads complete on the even CTA's `full` barrier; MMA completion is
+// multicast to both CTAs' `empty` / `tfull` barriers; both CTAs' epilogue
+// warps release the accumulator buffer on the even CTA's `tempty` barrier.
+constexpr int kStages2 = 6;
+constexpr int kHalfBytes = 128 * kBK;            // 16 KB: 128 rows x 128 K-bytes
+constexpr int kStageBytes2 = 2 * kHalfBytes;     // weights half + activations half
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster_addr, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+      : "memory");
+}
+template <int KIND>
+__device__ __forceinline__ void umma2(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  if (KIND == KIND_I8) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+  }
+}
+__device__ __forceinline__ void umma2_commit(uint64_t* bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(kThreadsTC, 1)
+    gemm_tc2_kernel(const __grid_constant__ TcParams p, const __grid_constant__ CUtensorMap mapW,
+                    const __grid_constant__ CUtensorMap mapX) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages2 * kStageBytes2);
+  uint64_t* empty = full + kStages2;
+  uint64_t* tfull = empty + kStages2;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader (issues the MMAs)
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int ntiles = p.tiles_w * p.tiles_x;  // tiles of 256 x 256
+  const int nkb = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages2; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_barrier();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const uint32_t full_leader = mapa_shared(smem_u32(full), 0);
+  const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
+
+  if (warp == 0) {
+    // ---- TMA producer (both CTAs): this CTA's halves, completing on the leader's barrier
+    if (lane == 0) {
+      prefetch_tensormap(&mapW);
+      prefetch_tensormap(&mapX);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < ntiles && ok; tile += npairs) {
+        const int tw = tile % p.tiles_w, tx = tile / p.tiles_w;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY))) break;
+          uint8_t* sw = smem + stage * kStageBytes2;
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes2);
+          const uint32_t fb = full_leader + stage * 8;
+          tma_load_2d_pair(sw, &mapW, fb, kb * kBK, tw * 256 + 128 * (int)rank);
+          tma_load_2d_pair(sw + kHalfBytes, &mapX, fb, kb * kBK, tx * 256 + 128 * (int)rank);
+          if (++stage == kStages2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      for (int s = 0; s < kStages2 && ok; ++s) {  // drain: all issued loads consumed
+        ok = mbar_wait(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY);
+        if (++stage == kStages2) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer (leader only)
+    if (rank == 0 && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      for (int tile = pair; tile < ntiles && ok; tile += npairs, ++it) {
+        const int buf = it & 1;
+        if (!(ok = mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1u, ERR_WAIT_TMEM_EMPTY))) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * 256);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!(ok = mbar_wait(&full[stage], phase, ERR_WAIT_FULL))) break;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kStageBytes2);
+          const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + kHalfBytes);
+#pragma unroll
+          for (int j = 0; j < kBK / 32; ++j)
+            umma2<KIND>(d_tmem, adesc + 2 * j, bdesc + 2 * j, p.idesc, (kb | j) != 0);
+          umma2_commit(&empty[stage], 0x3);
+          if (++stage == kStages2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        umma2_commit(&tfull[buf], 0x3);
+      }
+      umma2_commit(drain, 0x1);
+      mbar_wait(drain, 0, ERR_WAIT_FULL);
+    }
+  } else {
+    // ---- epilogue (both CTAs): this CTA's 128 TMEM lanes = 128 weight columns
+    const int q = warp & 3;
+    int it = 0;
+    for (int tile = pair; tile < ntiles; tile += npairs, ++it) {
+      const int buf = it & 1;
+      const int tw = tile % p.tiles_w, tx = tile / p.tiles_w;
+      if (!mbar_wait(&tfull[buf], (it >> 1) & 1, ERR_WAIT_TMEM_FULL)) break;
+      tc_fence_after();
+      const int n = tw * 256 + 128 * (int)rank + q * 32 + lane;
+      const bool nok = n < p.N;
+      float cs = 1.0f;
+      if (nok && KIND == KIND_I8) {
+        uint16_t sb = p.scale_tex ? tex1Dfetch<unsigned short>((cudaTextureObject_t)p.scale_tex, n) : p.scale_u16[n];
+        cs = __half2float(__ushort_as_half(sb));
+      }
+      const float cs2 = (nok && p.col_scale_f32) ? p.col_scale_f32[n] : 1.0f;
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
+      uint16_t* D = static_cast<uint16_t*>(p.D);
+#pragma unroll 1
+      for (int j0 = 0; j0 < 256; j0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + j0, r);
+        const int mbase = tx * 256 + j0;
+        if (!nok || mbase >= p.M) continue;
+        uint16_t o[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int m = mbase + j;
+          float v;
+          if (KIND == KIND_I8) {
+            float se = cs * (p.row_g ? p.row_g[m < p.M ? m : 0] : p.global_scale);
+            if (p.col_scale_f32) se = se * cs2;
+            v = (float)(int32_t)r[j] * se;
+          } else {
+            float rs = p.row_g ? p.row_g[m < p.M ? m : 0] : 1.0f;
+            v = __uint_as_float(r[j]) * rs * cs2;
+          }
+          o[j] = store_val(v, p.out_bf16);
+        }
+        const int mcount = min(32, p.M - mbase);
+        if (p.out_row_major) {
+          for (int j = 0; j < mcount; ++j) D[(size_t)(mbase + j) * p.N + n] = o[j];
+        } else {
+          uint16_t* dst = D + (size_t)n * p.M + mbase;
+          if (mcount == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
+#pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4) {
+              uint4 w;
+              w.x = (uint32_t)o[8 * v4 + 0] | ((uint32_t)o[8 * v4 + 1] << 16);
+              w.y = (uint32_t)o[8 * v4 + 2] | ((uint32_t)o[8 * v4 + 3] << 16);
+              w.z = (uint32_t)o[8 * v4 + 4] | ((uint32_t)o[8 * v4 + 5] << 16);
+              w.w = (uint32_t)o[8 * v4 + 6] | ((uint32_t)o[8 * v4 + 7] << 16);
+              reinterpret_cast<uint4*>(dst)[v4] = w;
+            }
+          } else {
+            for (int j = 0; j < mcount; ++j) dst[j] = o[j];
+          }
+        }
+        if (KIND == KIND_I8 && p.acc_out) {
+          for (int j = 0; j < mcount; ++j) p.acc_out[(size_t)n * p.M + mbase + j] = (int32_t)r[j];
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(tempty_leader + buf * 8);
+    }
+  }
+
+  tc_fence_before();
+  cluster_barrier();  // no CTA leaves while its pair may still use its smem or TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+  }
+}
+
+// M=256 instruction descriptor for the pair MMA
+template <int KIND>
+__host__ __device__ constexpr uint32_t make_idesc2(int a_fmt) {
+  return (KIND == KIND_I8 ? (2u << 4) | (1u << 7) | (1u << 10) : (1u << 4) | ((uint32_t)a_fmt << 7)) |
+         ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+
+bool g_use_pair = true;
+
+template <int KIND>
+cudaError_t launch_tc2(TcParams p, const void* W, const void* X, int a_fmt, cudaStream_t stream) {
+  CUtensorMap mw, mx;
+  cudaError_t e;
+  if ((e = make_tmap_2d_u8(&mw, W, p.K, p.N, p.K, kBK, 128, true)) != cudaSuccess) return e;
+  if ((e = make_tmap_2d_u8(&mx, X, p.K, p.M, p.K, kBK, 128, true)) != cudaSuccess) return e;
+  p.tiles_w = (p.N + 255) / 256;
+  p.tiles_x = (p.M + 255) / 256;
+  p.idesc = make_idesc2<KIND>(a_fmt);
+  auto kern = gemm_tc2_kernel<KIND>;
+  const int smem = kStages2 * kStageBytes2 + 1024 + 256;
+  if ((e = ensure_smem_attr((const void*)kern, smem)) != cudaSuccess) return e;
+  const int ntiles = p.tiles_w * p.tiles_x;
+  const int maxpairs = num_sms_current() / 2;
+  const int pairs = ntiles < maxpairs ? ntiles : maxpairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kThreadsTC, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p, mw, mx);
+}
+
 int grid_for(size_t work_items) {
   const int sms = num_sms_current();
   size_t blocks = (work_items + 255) / 256;
@@ -460,6 +743,8 @@ cudaError_t launch_tc(const TcParams& p, const CUtensorMap& mw, const CUtensorMa
 }
 
 }  // namespace
+
+void tc_set_pair_mode(bool on) { g_use_pair = on; }
 
 unsigned int tc_device_error(bool clear) {
   unsigned int v = 0;
@@ -524,6 +809,7 @@ cudaError_t launch_gemm_tc_s8(const GemvParams& gp, int a_type, int fmt, void* s
   p.acc_out = gp.acc_out;
   p.out_bf16 = gp.out_bf16;
   p.out_row_major = gp.out_row_major;
+  if (g_use_pair) return launch_tc2<KIND_I8>(p, Bq, Aq, 0, stream);
   return launch_tc<KIND_I8>(p, mw, mx, stream);
 }
 
@@ -562,6 +848,7 @@ cudaError_t launch_gemm_tc_fp8(const void* A, int a_type, const uint8_t* B, int 
   p.D = D;
   p.out_bf16 = out_bf16;
   p.out_row_major = out_row_major;
+  if (g_use_pair) return launch_tc2<KIND_F8>(p, B, Aq, b_fmt == 1 ? 1 : 0, stream);
   return launch_tc<KIND_F8>(p, mw, mx, stream);
 }
 

@@ -94,6 +94,9 @@ int fp8imma_fp8wgt_linear_forward(const void* A_f16, const void* B_u8, float sca
 int fp8imma_set_splitk(int splits);
 // Largest M routed to the small-M split-K kernel (default 64).
 int fp8imma_set_small_m_max(int m);
+// Large-M tensor-core kernel: 1 (default) = CTA-pair kernel (tcgen05
+// cta_group::2, 256x256 tiles), 0 = single-CTA kernel (128x256 tiles).
+int fp8imma_set_tc_pair(int enable);
 // Programmatic dependent launch (default off). When on, a GEMM may start
 // streaming its weights and reading its column scales while the previous
 // kernel in the stream is still running; activations are read, and outputs

@@ -18,10 +18,18 @@ pytestmark = pytest.mark.gpu
 TC_PATH, GEMV_PATH, NATIVE_PATH, NATIVE_SK_PATH = 3, 1, 4, 5
 
 
+@pytest.fixture(params=[1, 0], ids=["pair", "single"])
+def tc_mode(request, cuda):
+    L = F.lib()
+    L.fp8imma_set_tc_pair(request.param)
+    yield request.param
+    L.fp8imma_set_tc_pair(1)
+
+
 @pytest.mark.parametrize("variant", ["v4_f16", "v4_bf16", "v3_f16", "v2"])
 @pytest.mark.parametrize("M,N,K", [(128, 256, 512), (256, 128, 1024), (300, 200, 256), (513, 384, 2048),
                                    (1024, 1024, 1024), (65, 640, 128)])
-def test_tc_reference_api_bitexact(cuda, variant, M, N, K):
+def test_tc_reference_api_bitexact(tc_mode, variant, M, N, K):
     L = F.lib()
     A, B, s = np_inputs(variant, M, N, K, seed=M + N + K)
     err_o, D_o, _ = O.imma_fp8(variant, 32, A, B, s, 0.37, 9.5, nthreads=16)
@@ -49,7 +57,7 @@ def test_tc_special_scales_and_codes(cuda):
 
 @pytest.mark.parametrize("a_bf16,fmt,row_quant,out_row", [(False, "e4m3", False, False), (True, "e4m3", True, True),
                                                            (False, "e5m2", True, False), (True, "e5m2", False, True)])
-def test_tc_extended_args_and_accumulators(cuda, a_bf16, fmt, row_quant, out_row):
+def test_tc_extended_args_and_accumulators(tc_mode, a_bf16, fmt, row_quant, out_row):
     e = F.ext()
     from test_gpu_ext import inputs
 
@@ -68,7 +76,7 @@ def test_tc_extended_args_and_accumulators(cuda, a_bf16, fmt, row_quant, out_row
     assert bits_equal(to_np_bits(D), D_o, is_bf16=a_bf16).all()
 
 
-def test_tc_full_size_square4096_row_slices_and_splitk_agreement(cuda):
+def test_tc_full_size_square4096_row_slices_and_splitk_agreement(tc_mode):
     """M=N=K=4096 (square config): every output checked bitwise against the
     independent split-K kernel, and 48 rows against the CPU oracle."""
     from fp8imma_b200 import workloads as WL
@@ -103,7 +111,7 @@ def test_tc_full_size_square4096_row_slices_and_splitk_agreement(cuda):
                                                (1024, 512, 2048, "e4m3", True), (64, 384, 256, "e4m3", False),
                                                (1, 4096, 4096, "e4m3", False), (16, 1000, 1024, "e5m2", True),
                                                (33, 640, 512, "e4m3", False)])
-def test_native_fp8_matches_oracle(cuda, M, N, K, fmt, a_bf16):
+def test_native_fp8_matches_oracle(tc_mode, M, N, K, fmt, a_bf16):
     """Native FP8 path tolerance: fp16 outputs within 2e-3 relative (to the
     output's max magnitude) of the oracle, which uses the same quantised
     activations and exact (double) accumulation."""
