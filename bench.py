@@ -251,16 +251,31 @@ def main():
     barrier()
     path_id = ext.last_path()
 
-    # timed region: K steps (CUDA graph at N=1, eager with NCCL at N>1)
+    # timed region: K steps captured in one CUDA graph (the NCCL all-gather of
+    # the sharded layer included); eager launches if capture is refused
     stream = torch.cuda.Stream()
     graph = None
-    if world == 1:
-        torch.cuda.synchronize()
+    timing = "CUDA graph of K steps"
+    try:
+        if world > 1:
+            # NCCL inside a captured graph did not shorten the step here and
+            # made process-group teardown stall; the sharded step runs eagerly
+            raise RuntimeError("eager at N>1")
+        barrier()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
             for i in range(args.steps):
                 step(i)
         torch.cuda.synchronize()
+        graph.replay()
+        barrier()
+    except Exception as ex:  # capture not possible here: fall back to eager launches
+        graph = None
+        timing = "eager launches" if world > 1 else "eager launches (graph capture failed: %s)" % type(ex).__name__
+        torch.cuda.synchronize()
+        barrier()
+    if world > 1:
+        timing += ", NCCL all-gather in step"
     sampler = ClockSampler(local)
     sampler.start()
     # keep the GPU busy ~0.6 s so the clock samples reflect the loaded state
@@ -384,7 +399,7 @@ def main():
                        "weights": "E4M3 bytes, sigma_w=%g, per-column scales" % w["sigma_w"],
                        "path": "int8-exact (reference v4 semantics)", "parallelism": "column-parallel x%d" % world,
                        "l2": "weights rotated over %d copies (%.0f MB > 2x L2)" % (copies, copies * wbytes / 1e6),
-                       "timing": "CUDA graph of K steps" if world == 1 else "eager, NCCL all-gather in step",
+                       "timing": timing,
                        "pdl": bool(args.pdl)},
             "tflops": round(tflops, 4),
             "roofline": dict(roof, traffic=traffic),
