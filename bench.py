@@ -200,6 +200,8 @@ def main():
     ap.add_argument("--no-ref-lib", action="store_true")
     ap.add_argument("--points", action="store_true", help="also time the other decode/70B shapes")
     ap.add_argument("--pdl", action="store_true", help="launch with programmatic dependent launch")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="N>1: in-kernel NVLink gather (peer) or NCCL all-gather")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     w = WORKLOADS[args.workload]
@@ -235,7 +237,16 @@ def main():
     D_loc = D_full.narrow(0, rank * Nl, Nl)
     gs, ainv = 1.0 / 16.0, 16.0
 
+    fused = None
+    if world > 1 and args.gather == "peer" and M <= 64:
+        from fp8imma_b200.sharded import FusedGatherFP8Gemm
+
+        fused = FusedGatherFP8Gemm(B, s16, M)
+
     def step(i):
+        if fused is not None:
+            fused(A, gs, ainv, B=Bs[i % copies])
+            return
         ext.imma_fp8_gemm(A, Bs[i % copies], s16, None, gs, ainv, "tensor", "e4m3", "int8", "float16", "col", False,
                           D_loc)
         if world > 1:
@@ -257,9 +268,9 @@ def main():
     graph = None
     timing = "CUDA graph of K steps"
     try:
-        if world > 1:
+        if world > 1 and fused is None:
             # NCCL inside a captured graph did not shorten the step here and
-            # made process-group teardown stall; the sharded step runs eagerly
+            # made process-group teardown stall; that variant runs eagerly
             raise RuntimeError("eager at N>1")
         barrier()
         graph = torch.cuda.CUDAGraph()
@@ -275,7 +286,7 @@ def main():
         torch.cuda.synchronize()
         barrier()
     if world > 1:
-        timing += ", NCCL all-gather in step"
+        timing += ", in-kernel NVLink gather + flag barrier" if fused is not None else ", NCCL all-gather in step"
     sampler = ClockSampler(local)
     sampler.start()
     # keep the GPU busy ~0.6 s so the clock samples reflect the loaded state
@@ -334,6 +345,10 @@ def main():
 
     def e2e_step(i):
         A_dev.copy_(A_host[i % 4], non_blocking=True)
+        if fused is not None:
+            Df = fused(A_dev, gs, ainv, B=Bs[i % copies])
+            D_host.copy_(Df.narrow(0, rank * Nl, Nl), non_blocking=True)
+            return
         if use_v4:
             D = ext.imma_fp8_v4_act(A_dev, Bs[i % copies], s16, gs, ainv, 32)
         else:

@@ -329,7 +329,9 @@ int fp8imma_set_pdl(int enable) {
   return 0;
 }
 
-unsigned int fp8imma_device_error(int clear) { return gemv_device_error(clear != 0) | tc_device_error(clear != 0); }
+unsigned int fp8imma_device_error(int clear) {
+  return gemv_device_error(clear != 0) | tc_device_error(clear != 0) | peer_device_error(clear != 0);
+}
 
 const char* fp8imma_version(void) { return "fp8imma-b200 0.1 (sm_100a)"; }
 

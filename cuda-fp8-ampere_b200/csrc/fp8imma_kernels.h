@@ -62,6 +62,13 @@ void tc_set_pair_mode(bool on);  // tcgen05 GEMM: CTA-pair (cta_group::2) kernel
 cudaError_t launch_quant_a_e4m3(const void* A, int a_type, int M, int K, uint8_t* Aq, float* row_scale,
                                 cudaStream_t stream);
 
+// Push this rank's rows [row0, row0+rows) of a [*, M] fp16 buffer into every
+// peer's buffer at the same rows, then wait until every peer has done the
+// same (bounded wait; a timeout records a code and returns).
+cudaError_t launch_peer_gather(const unsigned long long* outs, const unsigned long long* pads, int world, int rank,
+                               size_t row0, size_t rows, int M, unsigned int epoch, cudaStream_t stream);
+unsigned int peer_device_error(bool clear);
+
 // Exact fallback for shapes the fast kernels do not take (any K, any alignment).
 cudaError_t launch_generic_s8(const GemvParams& p, int a_type, int fmt, cudaStream_t stream);
 

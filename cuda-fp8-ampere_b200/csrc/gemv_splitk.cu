@@ -409,8 +409,11 @@ __global__ void __launch_bounds__(kThreads, 3)
         if (p.acc_out) p.acc_out[(size_t)n * p.M + m] = sum[j];
       }
       const uint16_t o = store_val(v, p.out_bf16);
-      if (p.out_row_major) D[(size_t)m * p.N + n] = o;
-      else D[(size_t)n * p.M + m] = o;
+      if (p.out_row_major) {
+        D[(size_t)m * p.N + n] = o;
+      } else {
+        D[(size_t)n * p.M + m] = o;
+      }
     }
   }
   if (threadIdx.x == 0) TRACE_POINT(p, 7);

@@ -77,3 +77,73 @@ class ColumnParallelFP8Gemm:
             parts = list(out_full.chunk(self.world, dim=0))
             dist.all_gather(parts, mine.clone(), group=self.group)
         return out_full
+
+
+class FusedGatherFP8Gemm:
+    """Column-parallel GEMM whose output gather is fused into the kernel
+    (fp8imma_gemm_allgather): each rank's epilogue writes its output rows into
+    every rank's full output over NVLink, then a flag barrier. The full
+    outputs and the signal pad live in torch symmetric memory; two output
+    buffers alternate so a call never overwrites what a peer may still read.
+    Returns the full col-major D [N_total, M] (a view of the current buffer).
+    Small M only (the split-K kernel), int8-exact path, per-tensor scales.
+    """
+
+    def __init__(self, B_local: torch.Tensor, scales_local: torch.Tensor, M: int, group=None):
+        import ctypes
+
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import FP8ImmaGemmArgs, lib
+
+        self._ctypes, self._Args, self._lib = ctypes, FP8ImmaGemmArgs, lib()
+        self.group = group or dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        if self.world > 8:
+            raise ValueError("at most 8 ranks")
+        self.B = B_local.contiguous()
+        self.scales = scales_local.contiguous()
+        self.n_local = self.B.shape[0]
+        self.M = M
+        dev = self.B.device
+        name = self.group.group_name
+        try:
+            symm_mem.enable_symm_mem_for_group(name)
+        except Exception:
+            pass
+        self.bufs, self.handles = [], []
+        for _ in range(2):
+            t = symm_mem.empty(self.n_local * self.world, M, dtype=torch.float16, device=dev)
+            self.bufs.append(t)
+            self.handles.append(symm_mem.rendezvous(t, name))
+        self.pad = symm_mem.empty(64, dtype=torch.int32, device=dev)
+        self.pad.zero_()
+        pad_h = symm_mem.rendezvous(self.pad, name)
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        P = ctypes.c_void_p * self.world
+        self._outs = [P(*[ctypes.c_void_p(x) for x in h.buffer_ptrs]) for h in self.handles]
+        self._pads = P(*[ctypes.c_void_p(x) for x in pad_h.buffer_ptrs])
+        self.epoch = 0
+
+    def __call__(self, A: torch.Tensor, global_scale: float = 1.0, a_inv_scale: float = 1.0,
+                 B: torch.Tensor | None = None) -> torch.Tensor:
+        """B optionally replaces the stored weight shard for this call (same shape)."""
+        assert A.shape[0] == self.M and A.is_contiguous()
+        Bw = self.B if B is None else B
+        assert Bw.shape == self.B.shape and Bw.is_contiguous()
+        self.epoch += 1
+        which = self.epoch & 1  # host-side alternation; the barrier epoch itself is counted on the device
+        a = self._Args()
+        a.path, a.a_type, a.b_format, a.act_quant = 0, {torch.float16: 0, torch.bfloat16: 1, torch.int8: 2}[A.dtype], 0, 0
+        a.out_type, a.out_layout = 0, 0
+        a.M, a.N, a.K = self.M, self.n_local, A.shape[1]
+        a.A, a.B, a.col_scales_u16 = A.data_ptr(), Bw.data_ptr(), self.scales.data_ptr()
+        a.global_scale, a.a_inv_scale = float(global_scale), float(a_inv_scale)
+        stream = self._ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        err = self._lib.fp8imma_gemm_allgather(self._ctypes.byref(a), self._outs[which], self._pads, self.world,
+                                               self.rank, 0, stream)
+        if err != 0:
+            raise RuntimeError("fp8imma_gemm_allgather failed, cudaError_t=%d" % err)
+        return self.bufs[which]

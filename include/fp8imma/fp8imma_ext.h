@@ -89,6 +89,26 @@ int fp8imma_gemm_rowquant_noalloc(const fp8imma_gemm_args* args, void* stream);
 int fp8imma_fp8wgt_linear_forward(const void* A_f16, const void* B_u8, float scale_b, void* C_f32,
                                   int M, int N, int K, void* stream);
 
+// Column-parallel GEMM with the output gather fused in (no reference
+// counterpart: the reference has no multi-GPU code). Rank `rank` of `world`
+// (<= 8) passes its weight shard (args->B, [N_shard, K]) and shard scales;
+// the GEMM writes this rank's [N_shard, M] slice of the col-major output into
+// rows rank*N_shard.. of its own full buffer peer_out[rank] ([world*N_shard,
+// M]), then a gather kernel copies the slice into every peer's buffer over
+// NVLink (peer stores) and waits until every rank's slice has arrived here.
+// peer_out / peer_signal hold device pointers to all ranks' buffers, valid in
+// this process (e.g. a symmetric allocation); each signal pad needs `world`
+// zero-initialised uint32 slots; `epoch` must grow by one per call (1, 2, ...),
+// or be 0: the epoch is then counted on the device in slot 32 of this rank's
+// own pad (pads need 33 slots), so a captured CUDA graph can be replayed.
+// Int8-exact path, per-tensor quantisation, col-major output, small M (the
+// split-K kernel). The call returns when the launches are queued; the output
+// is complete on every rank once this stream reaches the end of the call.
+// The caller must not rewrite an output buffer that a peer may still be
+// reading from the previous call (alternate two buffers).
+int fp8imma_gemm_allgather(const fp8imma_gemm_args* args, void* const* peer_out, void* const* peer_signal, int world,
+                           int rank, unsigned int epoch, void* stream);
+
 // Tuning / introspection (no reference counterpart).
 // Force the K split of the small-M kernel (0 = automatic; 1, 2, 4 or 8).
 int fp8imma_set_splitk(int splits);

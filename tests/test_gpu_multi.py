@@ -40,7 +40,18 @@ def _worker(rank, world, port, M, N, K, q):
         full, _ = F.ext().imma_fp8_gemm(inp.A, inp.B, inp.scales_u16, None, 1.0 / 16, 16.0, "tensor", "e4m3", "int8",
                                         "float16", "col", False, None)
         torch.cuda.synchronize()
-        q.put((rank, bool(torch.equal(D.view(torch.int16), full.view(torch.int16)))))
+        ok = bool(torch.equal(D.view(torch.int16), full.view(torch.int16)))
+        if M <= 64:
+            # fused in-kernel gather over NVLink: same bits, several calls in a row
+            from fp8imma_b200.sharded import FusedGatherFP8Gemm
+
+            fused = FusedGatherFP8Gemm(inp.B[n0:n1], inp.scales_u16[n0:n1], M)
+            for _ in range(3):
+                Df = fused(inp.A, 1.0 / 16, 16.0)
+                torch.cuda.synchronize()
+                ok = ok and bool(torch.equal(Df.view(torch.int16), full.view(torch.int16)))
+            ok = ok and F.lib().fp8imma_device_error(0) == 0
+        q.put((rank, ok))
     finally:
         dist.destroy_process_group()
 
