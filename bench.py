@@ -517,6 +517,11 @@ def time_points(ext, steps):
                                           "TFLOPS": round(2 * M * N * K / (ms * 1e-3) / 1e12, 3),
                                           "kernel_path": ext.last_path()}
             del g
+        ref = time_reference_lib(A, [B], s16, M, N, K, 1.0 / 16, 16.0, 3 if M > 64 else 50, 1)
+        if "ms_per_call" in ref:
+            ms = ref["ms_per_call"]
+            out["%s_reflib" % name] = {"us": round(ms * 1e3, 3), "GB/s": round(alg_bytes(M, N, K) / (ms * 1e-3) / 1e9, 1),
+                                       "TFLOPS": round(2 * M * N * K / (ms * 1e-3) / 1e12, 3)}
         del Bs, B, A
         torch.cuda.empty_cache()
     return out
