@@ -58,6 +58,8 @@ cudaError_t launch_gemm_tc_fp8(const void* A, int a_type, const uint8_t* B, int 
                                void* D, int M, int N, int K, int out_bf16, int out_row_major, void* scratch,
                                cudaStream_t stream);
 unsigned int tc_device_error(bool clear);
+cudaError_t launch_gemm_tc_wgt(const void* A_f16, const uint8_t* B, float scale_b, float* C, int M, int N, int K,
+                               void* scratch, cudaStream_t stream);
 void tc_set_pair_mode(bool on);  // tcgen05 GEMM: CTA-pair (cta_group::2) kernel or 1-CTA kernel
 cudaError_t launch_quant_a_e4m3(const void* A, int a_type, int M, int K, uint8_t* Aq, float* row_scale,
                                 cudaStream_t stream);

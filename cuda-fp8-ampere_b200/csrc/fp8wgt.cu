@@ -111,6 +111,15 @@ extern "C" int fp8imma_fp8wgt_linear_forward(const void* A, const void* B, float
   if ((reinterpret_cast<uintptr_t>(A) & 15u) || (reinterpret_cast<uintptr_t>(B) & 7u))
     return (int)cudaErrorInvalidValue;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (M > 64 && (reinterpret_cast<uintptr_t>(B) & 15u) == 0) {
+    // large M: weights decoded once to fp16, then tcgen05 kind::f16 (fp32 accumulate)
+    void* scratch = nullptr;
+    cudaError_t e = cudaMallocAsync(&scratch, (size_t)N * K * 2, st);
+    if (e != cudaSuccess) return (int)e;
+    e = launch_gemm_tc_wgt(A, static_cast<const uint8_t*>(B), scale_b, static_cast<float*>(C), M, N, K, scratch, st);
+    cudaError_t e2 = cudaFreeAsync(scratch, st);
+    return (int)(e != cudaSuccess ? e : e2);
+  }
   const int MB = M >= 32 ? 4 : (M + 7) / 8;
   dim3 grid((N + 15) / 16, (M + MB * 8 - 1) / (MB * 8));
   const uint16_t* a = static_cast<const uint16_t*>(A);

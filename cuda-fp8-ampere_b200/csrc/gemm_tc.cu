@@ -39,7 +39,7 @@ constexpr int kStageBytes = kBytesW + kBytesX;
 constexpr int kThreadsTC = 192;
 constexpr int kTmemCols = 512;
 
-enum { KIND_I8 = 0, KIND_F8 = 1 };
+enum { KIND_I8 = 0, KIND_F8 = 1, KIND_F16 = 2 };  // KIND_F16: fp8wgt (fp16 x fp16 -> fp32, CTA-pair kernel only)
 
 // ---------------------------------------------------------------- tcgen05 --
 
@@ -486,6 +486,12 @@ __device__ __forceinline__ void umma2(uint32_t tmem_d, uint64_t adesc, uint64_t 
         "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
         : "memory");
+  } else if (KIND == KIND_F16) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
   } else {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -632,6 +638,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         tmem_ld32(taddr + j0, r);
         const int mbase = tx * 256 + j0;
         if (!nok || mbase >= p.M) continue;
+        if (KIND == KIND_F16) {  // fp8wgt: fp32 accumulators straight to row-major C[m, n]
+          float* C = static_cast<float*>(p.D);
+          const int mc = min(32, p.M - mbase);
+          for (int j = 0; j < mc; ++j) C[(size_t)(mbase + j) * p.N + n] = __uint_as_float(r[j]);
+          continue;
+        }
         uint16_t o[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -687,7 +699,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 // M=256 instruction descriptor for the pair MMA
 template <int KIND>
 __host__ __device__ constexpr uint32_t make_idesc2(int a_fmt) {
-  return (KIND == KIND_I8 ? (2u << 4) | (1u << 7) | (1u << 10) : (1u << 4) | ((uint32_t)a_fmt << 7)) |
+  // kind::f16 (fp16 x fp16, fp32 accumulate): a/b format 0 = F16
+  return (KIND == KIND_I8 ? (2u << 4) | (1u << 7) | (1u << 10)
+                          : (1u << 4) | (KIND == KIND_F16 ? 0u : ((uint32_t)a_fmt << 7))) |
          ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
 
@@ -850,6 +864,53 @@ cudaError_t launch_gemm_tc_fp8(const void* A, int a_type, const uint8_t* B, int 
   p.out_row_major = out_row_major;
   if (g_use_pair) return launch_tc2<KIND_F8>(p, B, Aq, b_fmt == 1 ? 1 : 0, stream);
   return launch_tc<KIND_F8>(p, mw, mx, stream);
+}
+
+namespace {
+// fp8wgt weights -> fp16 (torch_ext/fp8wgt/fp8wgt_ext_cuda.cu:195-198):
+// fp16_rn(float(lut_e4m3[b]) * scale_b), 16 bytes in, 32 bytes out per step.
+__global__ void __launch_bounds__(256) decode_b_f16_kernel(const uint8_t* __restrict__ B, size_t n16, float sb,
+                                                           uint16_t* __restrict__ Bh) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x) {
+    const uint4 v = ldg_stream_v4(reinterpret_cast<const uint4*>(B) + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t b0 = (w[j] >> (16 * h)) & 0xFFu, b1 = (w[j] >> (16 * h + 8)) & 0xFFu;
+        const float f0 = __fmul_rn(__half2float(__ushort_as_half(ref_e4m3_bits(b0))), sb);
+        const float f1 = __fmul_rn(__half2float(__ushort_as_half(ref_e4m3_bits(b1))), sb);
+        uint32_t r;
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(f1), "f"(f0));
+        o[2 * j + h] = r;
+      }
+    }
+    uint4* dst = reinterpret_cast<uint4*>(Bh) + 2 * i;
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+}  // namespace
+
+// fp8wgt linear for large M: weights decoded once to fp16 (scratch, 2NK
+// bytes), then the CTA-pair tcgen05 GEMM with kind::f16 and an fp32 row-major
+// epilogue. K % 8 == 0 (16-byte TMA row pitch).
+cudaError_t launch_gemm_tc_wgt(const void* A_f16, const uint8_t* B, float scale_b, float* C, int M, int N, int K,
+                               void* scratch, cudaStream_t stream) {
+  uint16_t* Bh = static_cast<uint16_t*>(scratch);
+  const size_t n16 = (size_t)N * K / 16;
+  const int sms = num_sms_current();
+  decode_b_f16_kernel<<<sms * 8, 256, 0, stream>>>(B, n16, scale_b, Bh);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  TcParams p = {};
+  p.M = M;
+  p.N = N;
+  p.K = 2 * K;  // the pipeline works in bytes of K
+  p.D = C;
+  return launch_tc2<KIND_F16>(p, Bh, A_f16, 0, stream);
 }
 
 }  // namespace fp8imma_b200

@@ -71,7 +71,8 @@ def test_int8_activation_api(cuda):
     assert bits_equal(to_np_bits(D), D_o).all()
 
 
-@pytest.mark.parametrize("M,N,K", [(16, 64, 64), (32, 256, 512), (64, 128, 1024), (48, 80, 96)])
+@pytest.mark.parametrize("M,N,K", [(16, 64, 64), (32, 256, 512), (64, 128, 1024), (48, 80, 96), (128, 256, 512),
+                                   (304, 400, 1024), (1024, 512, 2048)])
 def test_fp8wgt_linear(cuda, M, N, K):
     w = F.wgt_ext()
     rng = np.random.default_rng(M * N)
