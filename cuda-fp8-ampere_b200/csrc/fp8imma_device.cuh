@@ -113,7 +113,9 @@ __device__ __forceinline__ uint16_t inv_scale_bits(uint16_t scale_bits) {
 
 // int8-exact formats (transcoded): FMT_E4M3_REF, FMT_E5M2; native FP8 formats
 // (fed to the tensor core as bytes): FMT_E4M3FN, FMT_NATIVE_E5M2.
-enum { FMT_E4M3_REF = 0, FMT_E5M2 = 1, FMT_E4M3FN = 2, FMT_NATIVE_E5M2 = 3 };
+// FMT_WGT: the fp8wgt linear (E4M3 weights decoded to fp16(lut * scale_b),
+// fp16 activations, fp32 accumulation).
+enum { FMT_E4M3_REF = 0, FMT_E5M2 = 1, FMT_E4M3FN = 2, FMT_NATIVE_E5M2 = 3, FMT_WGT = 4 };
 
 // Exact scalar path (any inverse scale): the reference chain byte by byte.
 template <int FMT>
@@ -202,6 +204,36 @@ __device__ __forceinline__ uint32_t transcode4(uint32_t x, bool fast, uint32_t f
     return transcode4_fast_e4m3(x, fscale);
   }
   return transcode4_exact<FMT>(x, inv_h);
+}
+
+// fp8wgt weight decode, 4 bytes -> two f16x2 (bytes 0,1 -> lo; 2,3 -> hi) of
+// fp16_rn(float(lut[b]) * s), lut the reference table (exponent 15: +-Inf for
+// mantissa 0, NaN otherwise).
+//   1. exponent-15 NaN codes become 0x7F / 0xFF (NaN in hardware E4M3FN);
+//   2. hardware decode, exact for exponent <= 14; 0x78 / 0xF8 give +-256;
+//   3. *256 in fp16 is exact for |v| <= 240 and turns +-256 into +-Inf;
+//   4. fp32 product with s/256 (exact power-of-two rescale of s, which the
+//      host guarantees) is the reference's fp32 product v*s, rounded once to
+//      fp32 and once to fp16 exactly as the reference does.
+__device__ __forceinline__ void wgt_decode4_fast(uint32_t x, float s256, uint32_t& lo, uint32_t& hi) {
+  uint32_t t = ((x & 0x7F7F7F7Fu) + 0x07070707u) & 0x80808080u;  // bit 7 set iff (b & 0x7F) >= 0x79
+  x |= t - (t >> 7);
+  const uint32_t k256 = 0x5C005C00u;
+  const uint32_t h01 = hmul2_rn(cvt_e4m3x2_f16x2(x & 0xFFFFu), k256);
+  const uint32_t h23 = hmul2_rn(cvt_e4m3x2_f16x2(x >> 16), k256);
+  const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+  const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(f01.y * s256), "f"(f01.x * s256));
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(f23.y * s256), "f"(f23.x * s256));
+}
+
+// Exact scalar form of the same decode (any scale).
+__device__ __forceinline__ void wgt_decode4_exact(uint32_t x, float s, uint32_t& lo, uint32_t& hi) {
+  float f[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) f[j] = __half2float(__ushort_as_half(ref_e4m3_bits((x >> (8 * j)) & 0xFFu))) * s;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(f[1]), "f"(f[0]));
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(f[3]), "f"(f[2]));
 }
 
 // ------------------------------------------------ activation quantisation --

@@ -32,6 +32,8 @@ struct GemvParams {
   int out_bf16;
   int out_row_major;
   int pdl;                          // launched with programmatic stream serialisation
+  float wgt_scale;                  // FMT_WGT: scale_b (or scale_b / 256 when wgt_fast)
+  int wgt_fast;                     // FMT_WGT: packed decode allowed for this scale
   unsigned long long* trace;        // FP8IMMA_TRACE builds only: per-CTA phase timestamps
 };
 

@@ -120,6 +120,23 @@ extern "C" int fp8imma_fp8wgt_linear_forward(const void* A, const void* B, float
     cudaError_t e2 = cudaFreeAsync(scratch, st);
     return (int)(e != cudaSuccess ? e : e2);
   }
+  if ((reinterpret_cast<uintptr_t>(B) & 15u) == 0) {
+    // small M: the TMA split-K kernel in its fp16 mode (weights decoded in
+    // registers, raw fp16 activations in shared memory, fp32 accumulation)
+    GemvParams p = {};
+    p.A = A;
+    p.B = static_cast<const uint8_t*>(B);
+    p.D = C;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.keff_a = K;
+    // packed decode multiplies by scale_b / 256, exact unless that is an fp32 subnormal
+    const float mag = scale_b < 0.0f ? -scale_b : scale_b;
+    p.wgt_fast = (mag == 0.0f || !(mag < 0x1p-117f)) ? 1 : 0;
+    p.wgt_scale = p.wgt_fast ? scale_b * 0.00390625f : scale_b;
+    return (int)launch_gemv_s8(p, A_F16, FMT_WGT, 0, st);
+  }
   const int MB = M >= 32 ? 4 : (M + 7) / 8;
   dim3 grid((N + 15) / 16, (M + MB * 8 - 1) / (MB * 8));
   const uint16_t* a = static_cast<const uint16_t*>(A);

@@ -94,6 +94,18 @@ __device__ __forceinline__ void mma_f8_16832(float (&c)[4], uint32_t a0, uint32_
 
 template <int FMT>
 __host__ __device__ constexpr bool is_native() { return FMT == FMT_E4M3FN || FMT == FMT_NATIVE_E5M2; }
+// fp32 accumulation (native FP8 and fp8wgt) instead of exact int32
+template <int FMT>
+__host__ __device__ constexpr bool is_float_acc() { return is_native<FMT>() || FMT == FMT_WGT; }
+
+__device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 
 __device__ __forceinline__ uint4 lds128(const void* p) {
   uint4 r;
@@ -169,6 +181,47 @@ __device__ __forceinline__ void quant_chunk(const GemvParams& p, int8_t* aq, int
   }
 }
 
+// FMT_WGT: copy fp16 A[m0 : m0+MR, k0 : k0+len] into shared memory as it is
+// (row stride `stride` bytes), zero-filling rows >= M and k >= kvalid.
+template <int MR>
+__device__ __forceinline__ void copy_chunk_f16(const GemvParams& p, uint8_t* a, int stride, int m0, int k0, int len,
+                                               int kvalid) {
+  constexpr int kBatch = 4;
+  const int items_per_row = len >> 3;  // 8 halves per item
+  const int total = MR * items_per_row;
+  for (int base = threadIdx.x; base < total; base += kBatch * kConsumers) {
+    uint4 v[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int it = base + j * kConsumers;
+      const int r = it / items_per_row, c = (it - r * items_per_row) << 3;
+      const int m = m0 + r, k = k0 + c;
+      v[j] = make_uint4(0u, 0u, 0u, 0u);
+      if (it < total && m < p.M && k < kvalid)
+        v[j] = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.A) + (size_t)m * p.K + k);
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int it = base + j * kConsumers;
+      if (it >= total) break;
+      const int r = it / items_per_row, c = (it - r * items_per_row) << 3;
+      *reinterpret_cast<uint4*>(a + r * stride + c * 2) = v[j];
+    }
+  }
+}
+
+template <int AT, int MR, int FMT>
+__device__ __forceinline__ void stage_chunk(const GemvParams& p, int8_t* aq, int stride, int m0, int k0, int len,
+                                            int kvalid) {
+  // fp16 mode: zero-fill up to the whole 128-wide weight block (the MMA reads
+  // it all, and 0 * stale NaN bits would not be 0)
+  if (FMT == FMT_WGT)
+    copy_chunk_f16<MR>(p, reinterpret_cast<uint8_t*>(aq), stride, m0, k0, (len + kBlockK - 1) & ~(kBlockK - 1),
+                       kvalid);
+  else
+    quant_chunk<AT, MR>(p, aq, stride, m0, k0, len, kvalid);
+}
+
 template <int AT, int MB, int FMT, bool FAST>
 __device__ __forceinline__ void consumer_loop(const GemvParams& p, int (&acc)[MB][4], const uint8_t* stages,
                                               uint64_t* full, uint64_t* empty, int8_t* aq, int astride, int m0,
@@ -189,7 +242,7 @@ __device__ __forceinline__ void consumer_loop(const GemvParams& p, int (&acc)[MB
       int k0 = kbeg + i * kBlockK;
       int len = min(p.kc, kend - k0);
       len = (len + 63) & ~63;
-      quant_chunk<AT, MR>(p, aq, astride, m0, k0, len, kend);
+      stage_chunk<AT, MR, FMT>(p, aq, astride, m0, k0, len, kend);
       named_bar_sync(1, kConsumers);
       if (i == 0 && threadIdx.x == 0) TRACE_POINT(p, 3);
     }
@@ -201,6 +254,35 @@ __device__ __forceinline__ void consumer_loop(const GemvParams& p, int (&acc)[MB
       const int c = (4 * h + t) ^ swz;
       uint4 w0 = lds128(st + rowA * kBlockK + (c << 4));
       uint4 w1 = lds128(st + rowB * kBlockK + (c << 4));
+      if (FMT == FMT_WGT) {
+        // lane holds logical k = 16t .. 16t+15 of this 64-wide half for rows
+        // A/B; MMA j takes logical 16t+4j .. 16t+4j+3 as physical {2t, 2t+1,
+        // 2t+8, 2t+9}, and the activations (raw fp16, 32 bytes per lane) the same
+        const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
+        uint32_t alo[4], ahi[4], blo[4], bhi[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (FAST) {
+            wgt_decode4_fast(wa[j], p.wgt_scale, alo[j], ahi[j]);
+            wgt_decode4_fast(wb[j], p.wgt_scale, blo[j], bhi[j]);
+          } else {
+            wgt_decode4_exact(wa[j], p.wgt_scale, alo[j], ahi[j]);
+            wgt_decode4_exact(wb[j], p.wgt_scale, blo[j], bhi[j]);
+          }
+        }
+        const uint8_t* arow = reinterpret_cast<const uint8_t*>(aq) + (koff + 64 * h + 16 * t) * 2;
+#pragma unroll
+        for (int nb = 0; nb < MB; ++nb) {
+          const uint8_t* ap = arow + (nb * 8 + g) * astride;
+          uint4 q0 = lds128(ap), q1 = lds128(ap + 16);
+          float(&fa)[4] = *reinterpret_cast<float(*)[4]>(&acc[nb][0]);
+          mma_f16_16816(fa, alo[0], blo[0], ahi[0], bhi[0], q0.x, q0.y);
+          mma_f16_16816(fa, alo[1], blo[1], ahi[1], bhi[1], q0.z, q0.w);
+          mma_f16_16816(fa, alo[2], blo[2], ahi[2], bhi[2], q1.x, q1.y);
+          mma_f16_16816(fa, alo[3], blo[3], ahi[3], bhi[3], q1.z, q1.w);
+        }
+        continue;
+      }
       uint32_t wa0 = tc4<FMT, FAST>(w0.x, fs0, inv0), wa1 = tc4<FMT, FAST>(w0.y, fs0, inv0);
       uint32_t wa2 = tc4<FMT, FAST>(w0.z, fs0, inv0), wa3 = tc4<FMT, FAST>(w0.w, fs0, inv0);
       uint32_t wb0 = tc4<FMT, FAST>(w1.x, fs1, inv1), wb1 = tc4<FMT, FAST>(w1.y, fs1, inv1);
@@ -246,7 +328,8 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int kbeg = blockIdx.y * p.k_per_cta;
   const int kend = min(p.K, kbeg + p.k_per_cta);
   const int nkb = kend > kbeg ? (kend - kbeg + kBlockK - 1) / kBlockK : 0;
-  const int astride = p.kc + 64;  // +64 B: conflict-free 16-byte fragment loads
+  // +64 B (int8) / +16 B (fp16): conflict-free 16-byte fragment loads
+  const int astride = FMT == FMT_WGT ? 2 * p.kc + 16 : p.kc + 64;
 
   if (threadIdx.x == 0) TRACE_POINT(p, 0);
   if (threadIdx.x == 0) {
@@ -280,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 3)
         const int r = i / lines_per_row, l = i - r * lines_per_row;
         asm volatile("prefetch.global.L2 [%0];" ::"l"(abase + (size_t)r * p.K * esz + ((size_t)l << 7)));
       }
-      if (!is_native<FMT>() && !p.scale_tex && lane <= 2)
+      if (!is_float_acc<FMT>() && !p.scale_tex && lane <= 2)
         asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(p.scale_u16 + tile_n0) + (lane - 1) * 128));
     }
     if (lane == 0) {
@@ -302,8 +385,8 @@ __global__ void __launch_bounds__(kThreads, 3)
     const bool ok0 = col0 < p.N, ok1 = col1 < p.N;
     // column scales are requested first; their latency overlaps the first
     // activation chunk's loads below
-    const uint16_t sb0 = (ok0 && !is_native<FMT>()) ? load_col_scale_bits(p, col0) : (uint16_t)0;
-    const uint16_t sb1 = (ok1 && !is_native<FMT>()) ? load_col_scale_bits(p, col1) : (uint16_t)0;
+    const uint16_t sb0 = (ok0 && !is_float_acc<FMT>()) ? load_col_scale_bits(p, col0) : (uint16_t)0;
+    const uint16_t sb1 = (ok1 && !is_float_acc<FMT>()) ? load_col_scale_bits(p, col1) : (uint16_t)0;
     const float cs0 = (ok0 && p.col_scale_f32) ? p.col_scale_f32[col0] : 1.0f;
     const float cs1 = (ok1 && p.col_scale_f32) ? p.col_scale_f32[col1] : 1.0f;
     if (p.pdl) pdl_wait();  // activations may come from the previous kernel
@@ -312,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 3)
     if (nkb > 0) {
       int len = min(p.kc, kend - kbeg);
       len = (len + 63) & ~63;
-      quant_chunk<AT, MR>(p, aq, astride, m0, kbeg, len, kend);
+      stage_chunk<AT, MR, FMT>(p, aq, astride, m0, kbeg, len, kend);
     }
     // epilogue constants staged in shared memory (no global loads at the end)
     float* sc_s = reinterpret_cast<float*>(smem + kScaleOffset);
@@ -325,10 +408,11 @@ __global__ void __launch_bounds__(kThreads, 3)
       cs_s[lc0 + 8] = cs1;
     }
     if (threadIdx.x < MR) reinterpret_cast<float*>(smem + kRowScaleOffset)[threadIdx.x] = rg;
-    const uint16_t inv0 = (ok0 && !is_native<FMT>()) ? inv_scale_bits(sb0) : (uint16_t)0x3C00u;
-    const uint16_t inv1 = (ok1 && !is_native<FMT>()) ? inv_scale_bits(sb1) : (uint16_t)0x3C00u;
+    const uint16_t inv0 = (ok0 && !is_float_acc<FMT>()) ? inv_scale_bits(sb0) : (uint16_t)0x3C00u;
+    const uint16_t inv1 = (ok1 && !is_float_acc<FMT>()) ? inv_scale_bits(sb1) : (uint16_t)0x3C00u;
     // CTA-uniform transcode choice; also the barrier that publishes chunk 0
-    const bool all_fast = named_bar_and(2, kConsumers, fast_ok<FMT>(inv0) && fast_ok<FMT>(inv1));
+    const bool lane_fast = FMT == FMT_WGT ? p.wgt_fast != 0 : (fast_ok<FMT>(inv0) && fast_ok<FMT>(inv1));
+    const bool all_fast = named_bar_and(2, kConsumers, lane_fast);
     if (threadIdx.x == 0) TRACE_POINT(p, 2);
     const uint32_t fs0 = fast_scale<FMT>(inv0), fs1 = fast_scale<FMT>(inv1);
     if (all_fast)
@@ -387,11 +471,11 @@ __global__ void __launch_bounds__(kThreads, 3)
       if (e < nelem) {
         for (int q = 0; q < S; ++q) {
           const int32_t v = cluster.map_shared_rank(part, q)[lc * MR + mr];
-          if (is_native<FMT>()) acc_f += __int_as_float(v);
+          if (is_float_acc<FMT>()) acc_f += __int_as_float(v);
           else acc_s += v;
         }
       }
-      sum[j] = is_native<FMT>() ? __float_as_int(acc_f) : acc_s;
+      sum[j] = is_float_acc<FMT>() ? __float_as_int(acc_f) : acc_s;
     }
 #pragma unroll
     for (int j = 0; j < kEpiBatch; ++j) {
@@ -399,6 +483,10 @@ __global__ void __launch_bounds__(kThreads, 3)
       const int lc = lcs[j], mr = mrs[j];
       const int n = tile_n0 + lc, m = m0 + mr;
       if (e >= nelem || n >= p.N || m >= p.M) continue;
+      if (FMT == FMT_WGT) {  // fp32 row-major output C[m][n]
+        static_cast<float*>(p.D)[(size_t)m * p.N + n] = __int_as_float(sum[j]);
+        continue;
+      }
       float v;
       if (is_native<FMT>()) {
         v = __int_as_float(sum[j]) * rg_s[mr] * cs_s[lc];
@@ -476,22 +564,23 @@ cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaSt
   p.k_per_cta = kper;
   const int kc_max = MR > 16 ? 512 : 1024;
   p.kc = kper < kc_max ? kper : kc_max;
-  size_t smem_a = (size_t)MR * (p.kc + 64);
+  size_t smem_a = fmt == FMT_WGT ? (size_t)MR * (2 * p.kc + 16) : (size_t)MR * (p.kc + 64);
   size_t smem_p = (size_t)kTileN * MR * 4;
   size_t smem = (size_t)kAqOffset + (smem_a > smem_p ? smem_a : smem_p) + 1024;  // + alignment slack
   CUtensorMap tmap;
   cudaError_t e = make_tmap_2d_u8(&tmap, p.B, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)p.K, kBlockK, kTileN,
                                   /*swizzle128=*/true);
   if (e != cudaSuccess) return e;
-  switch (a_type * 4 + fmt) {
-    case A_F16 * 4 + FMT_E4M3_REF: return launch_mb<A_F16, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_F16 * 4 + FMT_E5M2: return launch_mb<A_F16, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_BF16 * 4 + FMT_E4M3_REF: return launch_mb<A_BF16, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_BF16 * 4 + FMT_E5M2: return launch_mb<A_BF16, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_S8 * 4 + FMT_E4M3_REF: return launch_mb<A_S8, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_S8 * 4 + FMT_E5M2: return launch_mb<A_S8, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_S8 * 4 + FMT_E4M3FN: return launch_mb<A_S8, FMT_E4M3FN>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_S8 * 4 + FMT_NATIVE_E5M2: return launch_mb<A_S8, FMT_NATIVE_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
+  switch (a_type * 8 + fmt) {
+    case A_F16 * 8 + FMT_E4M3_REF: return launch_mb<A_F16, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_F16 * 8 + FMT_E5M2: return launch_mb<A_F16, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_BF16 * 8 + FMT_E4M3_REF: return launch_mb<A_BF16, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_BF16 * 8 + FMT_E5M2: return launch_mb<A_BF16, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_S8 * 8 + FMT_E4M3_REF: return launch_mb<A_S8, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_S8 * 8 + FMT_E5M2: return launch_mb<A_S8, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_S8 * 8 + FMT_E4M3FN: return launch_mb<A_S8, FMT_E4M3FN>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_S8 * 8 + FMT_NATIVE_E5M2: return launch_mb<A_S8, FMT_NATIVE_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_F16 * 8 + FMT_WGT: return launch_mb<A_F16, FMT_WGT>(p, tmap, MB, S, mchunks, smem, stream);
     default: return cudaErrorInvalidValue;
   }
 }

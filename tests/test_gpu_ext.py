@@ -89,6 +89,61 @@ def test_fp8wgt_linear(cuda, M, N, K):
     assert err < 1e-3, err
 
 
+@pytest.mark.parametrize("M", [16, 48, 64])
+@pytest.mark.parametrize("scale_b", [0.05, -3.0, 0.0, 1e-40, 3e-36, 7.0e4])
+def test_fp8wgt_decode_exact_all_codes(cuda, M, scale_b):
+    """One-hot activations (A[m,k] = 1 for k == m) make every output a single
+    decoded weight plus exact zeros, so the small-M path's decode and the scale
+    rounding are checked bit for bit, on both the packed and the scalar decode.
+    Columns 0..239 cycle through the 240 finite codes; columns 240..255 hold
+    one exponent-15 code each (Inf / NaN) at k = 0 and zeros elsewhere, so row
+    0 sees +-Inf or NaN and the other rows 0 * Inf = NaN (NaN against NaN)."""
+    w = F.wgt_ext()
+    N, K = 256, 256
+    A = np.zeros((M, K), np.float16)
+    A[np.arange(M), np.arange(M)] = 1.0
+    codes = np.arange(256, dtype=np.uint8)
+    finite = codes[(codes & 0x78) != 0x78]
+    special = codes[(codes & 0x78) == 0x78]
+    B = np.zeros((N, K), np.uint8)
+    for n in range(240):
+        B[n] = np.roll(np.resize(finite, K), n)
+    B[240:, 0] = special
+    C_o = O.fp8wgt(A.view(np.uint16), B, scale_b)
+    C = w.fp8_linear_forward(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), scale_b)
+    torch.cuda.synchronize()
+    C = C.cpu().numpy()
+    nan_o, nan_g = np.isnan(C_o), np.isnan(C)
+    assert (nan_o == nan_g).all(), (nan_o != nan_g).sum()
+    assert (C.view(np.uint32)[~nan_g] == C_o.view(np.uint32)[~nan_o]).all()
+
+
+@pytest.mark.parametrize("M,N,K,boff", [(1, 4096, 1024, 0), (5, 200, 528, 0), (40, 300, 256, 0),
+                                        (7, 64, 128, 8)])
+def test_fp8wgt_cabi_ragged_rows(cuda, M, N, K, boff):
+    """The C entry point takes any M (the torch wrapper asks for multiples of
+    16 like the reference); boff = 8 gives 8-byte aligned weights, which take
+    the unstaged kernel instead of the TMA one."""
+    import ctypes
+    from helpers import ptr, stream_ptr
+
+    rng = np.random.default_rng(M + K)
+    A = rng.standard_normal((M, K)).astype(np.float16)
+    B = rng.integers(0, 0x78, (N, K), dtype=np.uint8) | (rng.integers(0, 2, (N, K), dtype=np.uint8) << 7)
+    C_o = O.fp8wgt(A.view(np.uint16), B, 0.125)
+    dA = torch.from_numpy(A).cuda()
+    raw = torch.zeros(N * K + 16, dtype=torch.uint8, device="cuda")
+    dB = raw[boff:boff + N * K].view(N, K)
+    dB.copy_(torch.from_numpy(B))
+    C = torch.full((M, N), float("nan"), device="cuda")
+    err = F.lib().fp8imma_fp8wgt_linear_forward(ptr(dA), ptr(dB), 0.125, ptr(C), M, N, K, stream_ptr())
+    assert err == 0
+    torch.cuda.synchronize()
+    C = C.cpu().numpy()
+    err = np.abs(C - C_o).max() / max(np.abs(C_o).max(), 1e-6)
+    assert err < 1e-3, err
+
+
 def test_fp8linear_module(cuda):
     import fp8_linear
 
