@@ -311,6 +311,12 @@ int fp8imma_set_splitk(int splits) {
   return 0;
 }
 
+int fp8imma_set_stream_k(int enable) {
+  if (enable < 0 || enable > 2) return (int)cudaErrorInvalidValue;
+  gemv_set_stream_k(enable);
+  return 0;
+}
+
 int fp8imma_set_small_m_max(int m) {
   if (m < 0) return (int)cudaErrorInvalidValue;
   g_small_m_max.store(m);

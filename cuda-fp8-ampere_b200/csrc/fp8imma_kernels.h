@@ -34,6 +34,7 @@ struct GemvParams {
   int pdl;                          // launched with programmatic stream serialisation
   float wgt_scale;                  // FMT_WGT: scale_b (or scale_b / 256 when wgt_fast)
   int wgt_fast;                     // FMT_WGT: packed decode allowed for this scale
+  int no_alloc;                     // the launcher may not allocate device memory
   unsigned long long* trace;        // FP8IMMA_TRACE builds only: per-CTA phase timestamps
 };
 
@@ -51,6 +52,9 @@ int num_sms_current();
 // splits = 0 picks the K split from the shape.
 cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaStream_t stream);
 int gemv_pick_splits(int N, int K, int mchunks, int num_sms);
+// Small-M kernel form: 1 (default) = stream-K where the cluster form would
+// need more than one wave, else clusters; 2 = always stream-K; 0 = never.
+void gemv_set_stream_k(int mode);
 
 // Large-M tensor-core path (tcgen05). Scratch must hold
 // gemm_tc_scratch_bytes() bytes (16-byte aligned).

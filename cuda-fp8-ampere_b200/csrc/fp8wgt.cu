@@ -131,6 +131,7 @@ extern "C" int fp8imma_fp8wgt_linear_forward(const void* A, const void* B, float
     p.N = N;
     p.K = K;
     p.keff_a = K;
+    p.out_row_major = 1;  // epilogue walks the fp32 output row-major
     // packed decode multiplies by scale_b / 256, exact unless that is an fp32 subnormal
     const float mag = scale_b < 0.0f ? -scale_b : scale_b;
     p.wgt_fast = (mag == 0.0f || !(mag < 0x1p-117f)) ? 1 : 0;

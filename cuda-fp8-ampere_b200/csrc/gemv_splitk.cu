@@ -28,6 +28,9 @@
 
 #include <cooperative_groups.h>
 
+#include <atomic>
+#include <mutex>
+
 // Opt-in phase tracing (compile with -DFP8IMMA_TRACE): thread 0 of each CTA
 // records %globaltimer at fixed points into p.trace[cta * 16 + point].
 #ifdef FP8IMMA_TRACE
@@ -213,13 +216,72 @@ __device__ __forceinline__ void copy_chunk_f16(const GemvParams& p, uint8_t* a, 
 template <int AT, int MR, int FMT>
 __device__ __forceinline__ void stage_chunk(const GemvParams& p, int8_t* aq, int stride, int m0, int k0, int len,
                                             int kvalid) {
-  // fp16 mode: zero-fill up to the whole 128-wide weight block (the MMA reads
-  // it all, and 0 * stale NaN bits would not be 0)
+  // float-accumulating modes stage (zero-filled) up to the whole 128-wide
+  // weight block: a half past K may still be multiplied (by zero weights),
+  // and 0 * stale NaN bits would not be 0
+  if (is_float_acc<FMT>()) len = (len + kBlockK - 1) & ~(kBlockK - 1);
   if (FMT == FMT_WGT)
-    copy_chunk_f16<MR>(p, reinterpret_cast<uint8_t*>(aq), stride, m0, k0, (len + kBlockK - 1) & ~(kBlockK - 1),
-                       kvalid);
+    copy_chunk_f16<MR>(p, reinterpret_cast<uint8_t*>(aq), stride, m0, k0, len, kvalid);
   else
     quant_chunk<AT, MR>(p, aq, stride, m0, k0, len, kvalid);
+}
+
+// One 64-wide K half (h) of a staged 128-byte weight block: transcode (or
+// decode) this lane's 2 x 16 weight bytes and run the MMAs against the staged
+// activations at chunk offset koff.
+template <int AT, int MB, int FMT, bool FAST>
+__device__ __forceinline__ void mma_half(const GemvParams& p, int (&acc)[MB][4], const uint8_t* st, const int8_t* aq,
+                                         int astride, int koff, int h, int rowA, int rowB, int swz, int g, int t,
+                                         uint32_t fs0, uint32_t fs1, uint16_t inv0, uint16_t inv1) {
+  const int c = (4 * h + t) ^ swz;
+  uint4 w0 = lds128(st + rowA * kBlockK + (c << 4));
+  uint4 w1 = lds128(st + rowB * kBlockK + (c << 4));
+  if (FMT == FMT_WGT) {
+    // lane holds logical k = 16t .. 16t+15 of this 64-wide half for rows
+    // A/B; MMA j takes logical 16t+4j .. 16t+4j+3 as physical {2t, 2t+1,
+    // 2t+8, 2t+9}, and the activations (raw fp16, 32 bytes per lane) the same
+    const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
+    uint32_t alo[4], ahi[4], blo[4], bhi[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (FAST) {
+        wgt_decode4_fast(wa[j], p.wgt_scale, alo[j], ahi[j]);
+        wgt_decode4_fast(wb[j], p.wgt_scale, blo[j], bhi[j]);
+      } else {
+        wgt_decode4_exact(wa[j], p.wgt_scale, alo[j], ahi[j]);
+        wgt_decode4_exact(wb[j], p.wgt_scale, blo[j], bhi[j]);
+      }
+    }
+    const uint8_t* arow = reinterpret_cast<const uint8_t*>(aq) + (koff + 64 * h + 16 * t) * 2;
+#pragma unroll
+    for (int nb = 0; nb < MB; ++nb) {
+      const uint8_t* ap = arow + (nb * 8 + g) * astride;
+      uint4 q0 = lds128(ap), q1 = lds128(ap + 16);
+      float(&fa)[4] = *reinterpret_cast<float(*)[4]>(&acc[nb][0]);
+      mma_f16_16816(fa, alo[0], blo[0], ahi[0], bhi[0], q0.x, q0.y);
+      mma_f16_16816(fa, alo[1], blo[1], ahi[1], bhi[1], q0.z, q0.w);
+      mma_f16_16816(fa, alo[2], blo[2], ahi[2], bhi[2], q1.x, q1.y);
+      mma_f16_16816(fa, alo[3], blo[3], ahi[3], bhi[3], q1.z, q1.w);
+    }
+    return;
+  }
+  uint32_t wa0 = tc4<FMT, FAST>(w0.x, fs0, inv0), wa1 = tc4<FMT, FAST>(w0.y, fs0, inv0);
+  uint32_t wa2 = tc4<FMT, FAST>(w0.z, fs0, inv0), wa3 = tc4<FMT, FAST>(w0.w, fs0, inv0);
+  uint32_t wb0 = tc4<FMT, FAST>(w1.x, fs1, inv1), wb1 = tc4<FMT, FAST>(w1.y, fs1, inv1);
+  uint32_t wb2 = tc4<FMT, FAST>(w1.z, fs1, inv1), wb3 = tc4<FMT, FAST>(w1.w, fs1, inv1);
+  const int8_t* arow = aq + koff + 64 * h + 16 * t;
+#pragma unroll
+  for (int nb = 0; nb < MB; ++nb) {
+    uint4 q = lds128(arow + (nb * 8 + g) * astride);
+    if (is_native<FMT>()) {
+      float(&fa)[4] = *reinterpret_cast<float(*)[4]>(&acc[nb][0]);
+      mma_f8_16832<FMT>(fa, wa0, wb0, wa1, wb1, q.x, q.y);
+      mma_f8_16832<FMT>(fa, wa2, wb2, wa3, wb3, q.z, q.w);
+    } else {
+      mma_s8_16832(acc[nb], wa0, wb0, wa1, wb1, q.x, q.y);
+      mma_s8_16832(acc[nb], wa2, wb2, wa3, wb3, q.z, q.w);
+    }
+  }
 }
 
 template <int AT, int MB, int FMT, bool FAST>
@@ -250,63 +312,41 @@ __device__ __forceinline__ void consumer_loop(const GemvParams& p, int (&acc)[MB
     if (i == 0 && threadIdx.x == 0) TRACE_POINT(p, 4);
     const uint8_t* st = stages + stage * kStageBytes;
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int c = (4 * h + t) ^ swz;
-      uint4 w0 = lds128(st + rowA * kBlockK + (c << 4));
-      uint4 w1 = lds128(st + rowB * kBlockK + (c << 4));
-      if (FMT == FMT_WGT) {
-        // lane holds logical k = 16t .. 16t+15 of this 64-wide half for rows
-        // A/B; MMA j takes logical 16t+4j .. 16t+4j+3 as physical {2t, 2t+1,
-        // 2t+8, 2t+9}, and the activations (raw fp16, 32 bytes per lane) the same
-        const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
-        uint32_t alo[4], ahi[4], blo[4], bhi[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (FAST) {
-            wgt_decode4_fast(wa[j], p.wgt_scale, alo[j], ahi[j]);
-            wgt_decode4_fast(wb[j], p.wgt_scale, blo[j], bhi[j]);
-          } else {
-            wgt_decode4_exact(wa[j], p.wgt_scale, alo[j], ahi[j]);
-            wgt_decode4_exact(wb[j], p.wgt_scale, blo[j], bhi[j]);
-          }
-        }
-        const uint8_t* arow = reinterpret_cast<const uint8_t*>(aq) + (koff + 64 * h + 16 * t) * 2;
-#pragma unroll
-        for (int nb = 0; nb < MB; ++nb) {
-          const uint8_t* ap = arow + (nb * 8 + g) * astride;
-          uint4 q0 = lds128(ap), q1 = lds128(ap + 16);
-          float(&fa)[4] = *reinterpret_cast<float(*)[4]>(&acc[nb][0]);
-          mma_f16_16816(fa, alo[0], blo[0], ahi[0], bhi[0], q0.x, q0.y);
-          mma_f16_16816(fa, alo[1], blo[1], ahi[1], bhi[1], q0.z, q0.w);
-          mma_f16_16816(fa, alo[2], blo[2], ahi[2], bhi[2], q1.x, q1.y);
-          mma_f16_16816(fa, alo[3], blo[3], ahi[3], bhi[3], q1.z, q1.w);
-        }
-        continue;
-      }
-      uint32_t wa0 = tc4<FMT, FAST>(w0.x, fs0, inv0), wa1 = tc4<FMT, FAST>(w0.y, fs0, inv0);
-      uint32_t wa2 = tc4<FMT, FAST>(w0.z, fs0, inv0), wa3 = tc4<FMT, FAST>(w0.w, fs0, inv0);
-      uint32_t wb0 = tc4<FMT, FAST>(w1.x, fs1, inv1), wb1 = tc4<FMT, FAST>(w1.y, fs1, inv1);
-      uint32_t wb2 = tc4<FMT, FAST>(w1.z, fs1, inv1), wb3 = tc4<FMT, FAST>(w1.w, fs1, inv1);
-      const int8_t* arow = aq + koff + 64 * h + 16 * t;
-#pragma unroll
-      for (int nb = 0; nb < MB; ++nb) {
-        uint4 q = lds128(arow + (nb * 8 + g) * astride);
-        if (is_native<FMT>()) {
-          float(&fa)[4] = *reinterpret_cast<float(*)[4]>(&acc[nb][0]);
-          mma_f8_16832<FMT>(fa, wa0, wb0, wa1, wb1, q.x, q.y);
-          mma_f8_16832<FMT>(fa, wa2, wb2, wa3, wb3, q.z, q.w);
-        } else {
-          mma_s8_16832(acc[nb], wa0, wb0, wa1, wb1, q.x, q.y);
-          mma_s8_16832(acc[nb], wa2, wb2, wa3, wb3, q.z, q.w);
-        }
-      }
-    }
+    for (int h = 0; h < 2; ++h)
+      mma_half<AT, MB, FMT, FAST>(p, acc, st, aq, astride, koff, h, rowA, rowB, swz, g, t, fs0, fs1, inv0, inv1);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);
     if (++stage == kStages) {
       stage = 0;
       phase ^= 1u;
     }
+  }
+}
+
+// Epilogue of one output element from its reduced sum (int32 bits, or fp32
+// bits for the float-accumulating modes): scales, cast, store.
+template <int FMT>
+__device__ __forceinline__ void store_out(const GemvParams& p, int n, int m, int32_t sum, float sc, float cs,
+                                          float rg) {
+  if (FMT == FMT_WGT) {  // fp32 row-major output C[m][n]
+    static_cast<float*>(p.D)[(size_t)m * p.N + n] = __int_as_float(sum);
+    return;
+  }
+  float v;
+  if (is_native<FMT>()) {
+    v = __int_as_float(sum) * rg * cs;
+  } else {
+    float se = sc * rg;
+    if (p.col_scale_f32) se = se * cs;
+    v = (float)sum * se;
+    if (p.acc_out) p.acc_out[(size_t)n * p.M + m] = sum;
+  }
+  const uint16_t o = store_val(v, p.out_bf16);
+  uint16_t* D = static_cast<uint16_t*>(p.D);
+  if (p.out_row_major) {
+    D[(size_t)m * p.N + n] = o;
+  } else {
+    D[(size_t)n * p.M + m] = o;
   }
 }
 
@@ -448,7 +488,6 @@ __global__ void __launch_bounds__(kThreads, 3)
   const float* sc_s = reinterpret_cast<const float*>(smem + kScaleOffset);
   const float* cs_s = reinterpret_cast<const float*>(smem + kColScaleOffset);
   const float* rg_s = reinterpret_cast<const float*>(smem + kRowScaleOffset);
-  uint16_t* D = static_cast<uint16_t*>(p.D);
   constexpr int kEpiBatch = 4;  // partial-sum reads in flight per thread
   for (int base = threadIdx.x; base < nelem; base += kEpiBatch * kThreads) {
     int32_t sum[kEpiBatch];
@@ -483,25 +522,7 @@ __global__ void __launch_bounds__(kThreads, 3)
       const int lc = lcs[j], mr = mrs[j];
       const int n = tile_n0 + lc, m = m0 + mr;
       if (e >= nelem || n >= p.N || m >= p.M) continue;
-      if (FMT == FMT_WGT) {  // fp32 row-major output C[m][n]
-        static_cast<float*>(p.D)[(size_t)m * p.N + n] = __int_as_float(sum[j]);
-        continue;
-      }
-      float v;
-      if (is_native<FMT>()) {
-        v = __int_as_float(sum[j]) * rg_s[mr] * cs_s[lc];
-      } else {
-        float se = sc_s[lc] * rg_s[mr];
-        if (p.col_scale_f32) se = se * cs_s[lc];
-        v = (float)sum[j] * se;
-        if (p.acc_out) p.acc_out[(size_t)n * p.M + m] = sum[j];
-      }
-      const uint16_t o = store_val(v, p.out_bf16);
-      if (p.out_row_major) {
-        D[(size_t)m * p.N + n] = o;
-      } else {
-        D[(size_t)n * p.M + m] = o;
-      }
+      store_out<FMT>(p, n, m, sum[j], sc_s[lc], cs_s[lc], rg_s[mr]);
     }
   }
   if (threadIdx.x == 0) TRACE_POINT(p, 7);
@@ -509,38 +530,381 @@ __global__ void __launch_bounds__(kThreads, 3)
   if (threadIdx.x == 0) TRACE_POINT(p, 8);
 }
 
+// ---------------------------------------------------------------------------
+// Stream-K form (default). Persistent CTAs, two per SM, no clusters: the work
+// (m-chunk, 128-column tile, 64-wide K half) units are laid out tile-major and
+// CTA c takes units [c*U/G, (c+1)*U/G), so every SM gets the same number of
+// weight bytes to within one 8 KB half-block whatever N and K are. A CTA's
+// range is a run of segments, one per column tile it touches; only its first
+// and last segment can be a part of a tile. Whole tiles are finished from
+// registers; a part writes int32 (fp32 bits) partials to the CTA's global
+// slot, and the CTA that brings the tile's arrival counter to its contributor
+// count sums the slots (L2 reads) and stores the epilogue, then re-arms the
+// counter. No CTA ever waits for another.
+
+// (unit counts fit in int: the launcher keeps U below 2^31)
+__device__ __forceinline__ int sk_begin(int c, int U, int G) { return (int)((long long)c * U / G); }
+// the CTA whose range holds unit u
+__device__ __forceinline__ int sk_owner(int u, int U, int G) { return (int)(((long long)(u + 1) * G - 1) / U); }
+
+template <int AT, int MB, int FMT, bool FAST>
+__device__ __forceinline__ bool segment_loop(const GemvParams& p, int (&acc)[MB][4], const uint8_t* stages,
+                                             uint64_t* full, uint64_t* empty, int8_t* aq, int astride, int m0,
+                                             int hs, int he, int kseg0, int kvalid, uint32_t fs0, uint32_t fs1,
+                                             uint16_t inv0, uint16_t inv1, int warp, int lane, int& stage,
+                                             uint32_t& phase, bool ok) {
+  constexpr int MR = MB * 8;
+  const int g = lane >> 2, t = lane & 3;
+  const int rowA = warp * 16 + (g >> 1) + 4 * (g & 1);
+  const int rowB = rowA + 8;
+  const int swz = rowA & 7;
+  const int b0 = hs >> 1, b1 = (he + 1) >> 1;
+  for (int b = b0; b < b1; ++b) {
+    const int rel = (b - b0) * kBlockK;
+    const int koff = rel % p.kc;
+    if (koff == 0 && rel > 0) {
+      named_bar_sync(1, kConsumers);
+      const int k0 = kseg0 + rel;
+      int len = min(p.kc, kvalid - k0);
+      len = (len + 63) & ~63;
+      stage_chunk<AT, MR, FMT>(p, aq, astride, m0, k0, len, kvalid);
+      named_bar_sync(1, kConsumers);
+    }
+    if (ok) ok = mbar_wait(&full[stage], phase, ERR_WAIT_FULL);
+    const uint8_t* st = stages + stage * kStageBytes;
+    if (2 * b >= hs && 2 * b + 2 <= he) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        mma_half<AT, MB, FMT, FAST>(p, acc, st, aq, astride, koff, h, rowA, rowB, swz, g, t, fs0, fs1, inv0, inv1);
+    } else {  // a segment that starts or ends on an odd half
+      const int h = 2 * b < hs ? 1 : 0;
+      mma_half<AT, MB, FMT, FAST>(p, acc, st, aq, astride, koff, h, rowA, rowB, swz, g, t, fs0, fs1, inv0, inv1);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (++stage == kStages) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
+  return ok;
+}
+
 template <int AT, int MB, int FMT>
-cudaError_t launch_t(const GemvParams& p, const CUtensorMap& tmap, int S, int mchunks, size_t smem,
-                     cudaStream_t stream) {
-  auto kern = gemv_s8_splitk_kernel<AT, MB, FMT>;
-  cudaError_t e = ensure_smem_attr((const void*)kern, (int)smem);
-  if (e != cudaSuccess) return e;
+__global__ void __launch_bounds__(kThreads, 2)
+    gemv_streamk_kernel(const __grid_constant__ GemvParams p, const __grid_constant__ CUtensorMap tmap,
+                        int32_t* __restrict__ partials, unsigned int* __restrict__ counters) {
+  constexpr int MR = MB * 8;
+  constexpr int kSlot = kTileN * MR;  // int32 words per partial slot
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOffset);
+  uint64_t* empty = full + kStages;
+  int8_t* aq = reinterpret_cast<int8_t*>(smem + kAqOffset);
+  int32_t* part = reinterpret_cast<int32_t*>(smem + kAqOffset);  // whole-tile epilogue staging
+  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + kBarOffset + 2 * kStages * 8);
+  float* sc_s = reinterpret_cast<float*>(smem + kScaleOffset);
+  float* cs_s = reinterpret_cast<float*>(smem + kColScaleOffset);
+  float* rg_s = reinterpret_cast<float*>(smem + kRowScaleOffset);
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = gridDim.x;
+  const int cta = blockIdx.x;
+  const int tiles = (p.N + kTileN - 1) / kTileN;
+  const int hpt = (p.K + 63) >> 6;  // 64-wide K halves per tile
+  const int per_mc = (int)tiles * hpt;
+  const int U = per_mc * ((p.M + MR - 1) / MR);
+  const int ub = sk_begin(cta, U, G), ue = sk_begin(cta + 1, U, G);
+  const int astride = FMT == FMT_WGT ? 2 * p.kc + 16 : p.kc + 64;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ---- TMA producer: the same segment walk, one 16 KB block per stage
+    if (lane == 0) {
+      prefetch_tensormap(&tmap);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = ub; u < ue && ok;) {
+        const int rem = u % per_mc;
+        const int tile = (int)(rem / hpt), hs = (int)(rem % hpt);
+        const int se = min(ue, u - hs + hpt);
+        const int he = hs + (int)(se - u);
+        for (int b = hs >> 1; b < (he + 1) >> 1; ++b) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], kStageBytes);
+          tma_load_2d(stages + stage * kStageBytes, &tmap, &full[stage], b * kBlockK, tile * kTileN);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        u = se;
+      }
+    }
+    return;
+  }
+
+  // ---- consumers
+  if (threadIdx.x == 0) TRACE_POINT(p, 0);
+  if (p.pdl) pdl_wait();
+  const int g = lane >> 2, t = lane & 3;
+  const int lc0 = warp * 16 + (g >> 1) + 4 * (g & 1);
+  int stage = 0;
+  uint32_t phase = 0;
+  bool ok = true;
+  for (int u = ub; u < ue;) {
+    const int mcl = u / per_mc;
+    const int rem = u - mcl * per_mc;
+    const int tile = (int)(rem / hpt), hs = (int)(rem % hpt);
+    const int se = min(ue, u - hs + hpt);
+    const int he = hs + (int)(se - u);
+    const int tile_u0 = u - hs;
+    const int m0 = (int)mcl * MR, tile_n0 = tile * kTileN;
+    const int kseg0 = (hs >> 1) * kBlockK;
+    const int kvalid = min(p.K, he * 64);
+    const int col0 = tile_n0 + lc0, col1 = col0 + 8;
+    const bool ok0 = col0 < p.N, ok1 = col1 < p.N;
+    const uint16_t sb0 = (ok0 && !is_float_acc<FMT>()) ? load_col_scale_bits(p, col0) : (uint16_t)0;
+    const uint16_t sb1 = (ok1 && !is_float_acc<FMT>()) ? load_col_scale_bits(p, col1) : (uint16_t)0;
+    const float cs0 = (ok0 && p.col_scale_f32) ? p.col_scale_f32[col0] : 1.0f;
+    const float cs1 = (ok1 && p.col_scale_f32) ? p.col_scale_f32[col1] : 1.0f;
+    float rg = 0.0f;
+    if (threadIdx.x < MR && m0 + (int)threadIdx.x < p.M) rg = p.row_g ? p.row_g[m0 + threadIdx.x] : p.global_scale;
+    named_bar_sync(1, kConsumers);  // the previous segment is done with aq / part / the constants
+    {
+      int len = min(p.kc, kvalid - kseg0);
+      len = (len + 63) & ~63;
+      stage_chunk<AT, MR, FMT>(p, aq, astride, m0, kseg0, len, kvalid);
+    }
+    if ((lane & 3) == 0) {
+      sc_s[lc0] = __half2float(__ushort_as_half(sb0));
+      sc_s[lc0 + 8] = __half2float(__ushort_as_half(sb1));
+    } else if ((lane & 3) == 1) {
+      cs_s[lc0] = cs0;
+      cs_s[lc0 + 8] = cs1;
+    }
+    if (threadIdx.x < MR) rg_s[threadIdx.x] = rg;
+    const uint16_t inv0 = (ok0 && !is_float_acc<FMT>()) ? inv_scale_bits(sb0) : (uint16_t)0x3C00u;
+    const uint16_t inv1 = (ok1 && !is_float_acc<FMT>()) ? inv_scale_bits(sb1) : (uint16_t)0x3C00u;
+    const bool lane_fast = FMT == FMT_WGT ? p.wgt_fast != 0 : (fast_ok<FMT>(inv0) && fast_ok<FMT>(inv1));
+    const bool all_fast = named_bar_and(2, kConsumers, lane_fast);  // also publishes chunk 0
+    if (threadIdx.x == 0 && u == ub) TRACE_POINT(p, 2);
+    const uint32_t fs0 = fast_scale<FMT>(inv0), fs1 = fast_scale<FMT>(inv1);
+    int acc[MB][4];
+#pragma unroll
+    for (int i = 0; i < MB; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0;
+    if (all_fast)
+      ok = segment_loop<AT, MB, FMT, true>(p, acc, stages, full, empty, aq, astride, m0, hs, he, kseg0, kvalid, fs0,
+                                           fs1, inv0, inv1, warp, lane, stage, phase, ok);
+    else
+      ok = segment_loop<AT, MB, FMT, false>(p, acc, stages, full, empty, aq, astride, m0, hs, he, kseg0, kvalid, fs0,
+                                            fs1, inv0, inv1, warp, lane, stage, phase, ok);
+
+    if (threadIdx.x == 0 && u == ub) TRACE_POINT(p, 4);
+    const int nelem = kTileN * MR;
+    if (hs == 0 && he == hpt) {
+      // whole tile: registers -> shared memory -> epilogue
+      named_bar_sync(1, kConsumers);  // every warp is done reading aq
+#pragma unroll
+      for (int nb = 0; nb < MB; ++nb) {
+        *reinterpret_cast<int2*>(part + lc0 * MR + nb * 8 + 2 * t) = make_int2(acc[nb][0], acc[nb][1]);
+        *reinterpret_cast<int2*>(part + (lc0 + 8) * MR + nb * 8 + 2 * t) = make_int2(acc[nb][2], acc[nb][3]);
+      }
+      named_bar_sync(1, kConsumers);
+      for (int e = threadIdx.x; e < nelem; e += kConsumers) {
+        int lc, mr;
+        if (p.out_row_major || FMT == FMT_WGT) {
+          mr = e / kTileN;
+          lc = e - mr * kTileN;
+        } else {
+          lc = e / MR;
+          mr = e - lc * MR;
+        }
+        const int n = tile_n0 + lc, m = m0 + mr;
+        if (n < p.N && m < p.M) store_out<FMT>(p, n, m, part[lc * MR + mr], sc_s[lc], cs_s[lc], rg_s[mr]);
+      }
+    } else {
+      // part of a tile: partials -> this CTA's slot; the last arrival finishes
+      const int slot = ub >= tile_u0 ? 0 : 1;  // the tile is this CTA's first (0) or last (1) segment
+      int32_t* mine = partials + ((size_t)cta * 2 + slot) * kSlot;
+#pragma unroll
+      for (int nb = 0; nb < MB; ++nb) {
+        *reinterpret_cast<int2*>(mine + lc0 * MR + nb * 8 + 2 * t) = make_int2(acc[nb][0], acc[nb][1]);
+        *reinterpret_cast<int2*>(mine + (lc0 + 8) * MR + nb * 8 + 2 * t) = make_int2(acc[nb][2], acc[nb][3]);
+      }
+      named_bar_sync(1, kConsumers);
+      const int cf = sk_owner(tile_u0, U, G), cl = sk_owner(tile_u0 + hpt - 1, U, G);
+      if (threadIdx.x == 0) {
+        // acq_rel: releases this CTA's partials (ordered before by the barrier)
+        // and, for the last arrival, acquires every other contributor's
+        unsigned int* ctr = counters + mcl * tiles + tile;
+        unsigned int prev;
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ctr) : "memory");
+        const int last = prev == (unsigned int)(cl - cf);
+        if (last) *ctr = 0u;  // re-armed for the next call
+        *last_flag = last;
+      }
+      named_bar_sync(1, kConsumers);
+      if (threadIdx.x == 0 && u == ub) TRACE_POINT(p, 5);
+      if (*last_flag) {
+        // 4 consecutive rows of one column per thread, up to 8 contributors'
+        // 16-byte partials in flight at once
+        const int ncontrib = (int)(cl - cf + 1);
+        for (int qd = threadIdx.x; qd < kTileN * MR / 4; qd += kConsumers) {
+          const int lc = qd / (MR / 4), mr0 = (qd - lc * (MR / 4)) * 4;
+          int si[4] = {0, 0, 0, 0};
+          float sf[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          for (int j0 = 0; j0 < ncontrib; j0 += 4) {
+            int4 v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if (j0 + j < ncontrib) {
+                const int q = cf + j0 + j;
+                const int sl = sk_begin(q, U, G) >= tile_u0 ? 0 : 1;
+                v[j] = __ldcg(reinterpret_cast<const int4*>(partials + ((size_t)q * 2 + sl) * kSlot + lc * MR + mr0));
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if (j0 + j < ncontrib) {
+                if (is_float_acc<FMT>()) {
+                  sf[0] += __int_as_float(v[j].x);
+                  sf[1] += __int_as_float(v[j].y);
+                  sf[2] += __int_as_float(v[j].z);
+                  sf[3] += __int_as_float(v[j].w);
+                } else {
+                  si[0] += v[j].x;
+                  si[1] += v[j].y;
+                  si[2] += v[j].z;
+                  si[3] += v[j].w;
+                }
+              }
+            }
+          }
+          const int n = tile_n0 + lc;
+          if (n < p.N) {
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const int m = m0 + mr0 + r;
+              if (m < p.M)
+                store_out<FMT>(p, n, m, is_float_acc<FMT>() ? __float_as_int(sf[r]) : si[r], sc_s[lc], cs_s[lc],
+                               rg_s[mr0 + r]);
+            }
+          }
+        }
+      }
+    }
+    if (threadIdx.x == 0 && u == ub) TRACE_POINT(p, 6);
+    u = se;
+  }
+  if (threadIdx.x == 0) TRACE_POINT(p, 8);
+}
+
+struct LaunchShape {
+  int S, mchunks;
+  size_t smem;
+  int sk_grid;  // > 0: stream-K kernel on this many CTAs
+  int32_t* partials;
+  unsigned int* counters;
+};
+
+template <int AT, int MB, int FMT>
+cudaError_t launch_t(const GemvParams& p, const CUtensorMap& tmap, const LaunchShape& ls, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((p.N + kTileN - 1) / kTileN, S, mchunks);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = ls.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = S;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
   cfg.attrs = attr;
+  if (ls.sk_grid > 0) {
+    auto kern = gemv_streamk_kernel<AT, MB, FMT>;
+    cudaError_t e = ensure_smem_attr((const void*)kern, (int)ls.smem);
+    if (e != cudaSuccess) return e;
+    cfg.gridDim = dim3(ls.sk_grid, 1, 1);
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, p, tmap, ls.partials, ls.counters);
+  }
+  auto kern = gemv_s8_splitk_kernel<AT, MB, FMT>;
+  cudaError_t e = ensure_smem_attr((const void*)kern, (int)ls.smem);
+  if (e != cudaSuccess) return e;
+  cfg.gridDim = dim3((p.N + kTileN - 1) / kTileN, ls.S, ls.mchunks);
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = ls.S;
+  attr[1].val.clusterDim.z = 1;
   cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kern, p, tmap);
 }
 
 template <int AT, int FMT>
-cudaError_t launch_mb(const GemvParams& p, const CUtensorMap& tmap, int MB, int S, int mchunks, size_t smem,
-                      cudaStream_t st) {
+cudaError_t launch_mb(const GemvParams& p, const CUtensorMap& tmap, int MB, const LaunchShape& ls, cudaStream_t st) {
   switch (MB) {
-    case 1: return launch_t<AT, 1, FMT>(p, tmap, S, mchunks, smem, st);
-    case 2: return launch_t<AT, 2, FMT>(p, tmap, S, mchunks, smem, st);
-    case 3: return launch_t<AT, 3, FMT>(p, tmap, S, mchunks, smem, st);
-    default: return launch_t<AT, 4, FMT>(p, tmap, S, mchunks, smem, st);
+    case 1: return launch_t<AT, 1, FMT>(p, tmap, ls, st);
+    case 2: return launch_t<AT, 2, FMT>(p, tmap, ls, st);
+    case 3: return launch_t<AT, 3, FMT>(p, tmap, ls, st);
+    default: return launch_t<AT, 4, FMT>(p, tmap, ls, st);
   }
+}
+
+// Stream-K scratch: per device, allocated once (never while the stream is
+// being captured) and never freed, so captured graphs keep valid pointers. A
+// ring of kSkRing slots (arrival counters + partial sums) is handed out round
+// robin, so up to kSkRing calls may run at once on one device.
+constexpr int kSkRing = 4;
+constexpr int kSkMinUnits = 6;
+constexpr int kSkAutoUnits = 48;
+constexpr int kSkMaxCounters = 16384;  // m-chunks x column tiles per call
+constexpr int kSkMaxDevices = 64;
+std::mutex g_sk_mu;
+void* g_sk_base[kSkMaxDevices];
+size_t g_sk_part_bytes[kSkMaxDevices];
+std::atomic<unsigned int> g_sk_seq{0};
+std::atomic<int> g_stream_k{1};
+
+bool stream_k_scratch(cudaStream_t st, int grid_max, bool may_alloc, int32_t** part, unsigned int** ctr) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kSkMaxDevices) return false;
+  std::lock_guard<std::mutex> lk(g_sk_mu);
+  if (!g_sk_base[dev]) {
+    if (!may_alloc) return false;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return false;
+    const size_t part_bytes = (size_t)grid_max * 2 * kTileN * 32 * sizeof(int32_t);
+    const size_t slot = (size_t)kSkMaxCounters * 4 + part_bytes;
+    void* b = nullptr;
+    if (cudaMalloc(&b, slot * kSkRing) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    if (cudaMemset(b, 0, slot * kSkRing) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+      cudaFree(b);
+      cudaGetLastError();
+      return false;
+    }
+    g_sk_base[dev] = b;
+    g_sk_part_bytes[dev] = part_bytes;
+  }
+  if ((size_t)grid_max * 2 * kTileN * 32 * sizeof(int32_t) > g_sk_part_bytes[dev]) return false;
+  const unsigned int i = g_sk_seq.fetch_add(1u) % kSkRing;
+  char* s = static_cast<char*>(g_sk_base[dev]) + (size_t)i * ((size_t)kSkMaxCounters * 4 + g_sk_part_bytes[dev]);
+  *ctr = reinterpret_cast<unsigned int*>(s);
+  *part = reinterpret_cast<int32_t*>(s + (size_t)kSkMaxCounters * 4);
+  return true;
 }
 
 }  // namespace
@@ -557,33 +921,60 @@ cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaSt
   const int MB = p.M >= 32 ? 4 : (p.M + 7) / 8;
   const int MR = MB * 8;
   const int mchunks = (p.M + MR - 1) / MR;
-  int S = splits > 0 ? splits : gemv_pick_splits(p.N, p.K, mchunks, num_sms_current());
-  if (S != 1 && S != 2 && S != 4 && S != 8) return cudaErrorInvalidValue;
-  int kper = (p.K + S - 1) / S;
-  kper = (kper + 255) & ~255;
-  p.k_per_cta = kper;
+  const int tiles = (p.N + kTileN - 1) / kTileN;
   const int kc_max = MR > 16 ? 512 : 1024;
-  p.kc = kper < kc_max ? kper : kc_max;
+  LaunchShape ls = {};
+  ls.mchunks = mchunks;
+  const int sms = num_sms_current();
+  // stream-K only where every CTA gets at least kSkAutoUnits halves (its
+  // partial-tile fix-up, about 2 us, is then amortised): the large
+  // projections, where the cluster form's 2-per-SM waves are uneven
+  const long long all_units = (long long)mchunks * tiles * ((p.K + 63) / 64);
+  const bool big = all_units >= (long long)kSkAutoUnits * 2 * sms;
+  if (splits == 0 && g_stream_k.load() && (g_stream_k.load() == 2 || big) &&
+      (long long)tiles * mchunks <= kSkMaxCounters) {
+    const long long units = (long long)mchunks * tiles * ((p.K + 63) / 64);
+    // at least kSkMinUnits halves (48 KB of weights) per CTA keeps tiles to a few contributors
+    const long long want = (units + kSkMinUnits - 1) / kSkMinUnits;
+    const int grid = (int)(want < 2LL * sms ? want : 2LL * sms);
+    if (units < (1LL << 30) && stream_k_scratch(stream, 2 * sms, !p.no_alloc, &ls.partials, &ls.counters)) {
+      ls.sk_grid = grid;
+      const int kr = (p.K + kBlockK - 1) & ~(kBlockK - 1);
+      p.kc = kr < kc_max ? kr : kc_max;
+      p.k_per_cta = p.K;
+    }
+  }
+  if (ls.sk_grid == 0) {
+    int S = splits > 0 ? splits : gemv_pick_splits(p.N, p.K, mchunks, num_sms_current());
+    if (S != 1 && S != 2 && S != 4 && S != 8) return cudaErrorInvalidValue;
+    int kper = (p.K + S - 1) / S;
+    kper = (kper + 255) & ~255;
+    p.k_per_cta = kper;
+    p.kc = kper < kc_max ? kper : kc_max;
+    ls.S = S;
+  }
   size_t smem_a = fmt == FMT_WGT ? (size_t)MR * (2 * p.kc + 16) : (size_t)MR * (p.kc + 64);
   size_t smem_p = (size_t)kTileN * MR * 4;
-  size_t smem = (size_t)kAqOffset + (smem_a > smem_p ? smem_a : smem_p) + 1024;  // + alignment slack
+  ls.smem = (size_t)kAqOffset + (smem_a > smem_p ? smem_a : smem_p) + 1024;  // + alignment slack
   CUtensorMap tmap;
   cudaError_t e = make_tmap_2d_u8(&tmap, p.B, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)p.K, kBlockK, kTileN,
                                   /*swizzle128=*/true);
   if (e != cudaSuccess) return e;
   switch (a_type * 8 + fmt) {
-    case A_F16 * 8 + FMT_E4M3_REF: return launch_mb<A_F16, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_F16 * 8 + FMT_E5M2: return launch_mb<A_F16, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_BF16 * 8 + FMT_E4M3_REF: return launch_mb<A_BF16, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_BF16 * 8 + FMT_E5M2: return launch_mb<A_BF16, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_S8 * 8 + FMT_E4M3_REF: return launch_mb<A_S8, FMT_E4M3_REF>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_S8 * 8 + FMT_E5M2: return launch_mb<A_S8, FMT_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_S8 * 8 + FMT_E4M3FN: return launch_mb<A_S8, FMT_E4M3FN>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_S8 * 8 + FMT_NATIVE_E5M2: return launch_mb<A_S8, FMT_NATIVE_E5M2>(p, tmap, MB, S, mchunks, smem, stream);
-    case A_F16 * 8 + FMT_WGT: return launch_mb<A_F16, FMT_WGT>(p, tmap, MB, S, mchunks, smem, stream);
+    case A_F16 * 8 + FMT_E4M3_REF: return launch_mb<A_F16, FMT_E4M3_REF>(p, tmap, MB, ls, stream);
+    case A_F16 * 8 + FMT_E5M2: return launch_mb<A_F16, FMT_E5M2>(p, tmap, MB, ls, stream);
+    case A_BF16 * 8 + FMT_E4M3_REF: return launch_mb<A_BF16, FMT_E4M3_REF>(p, tmap, MB, ls, stream);
+    case A_BF16 * 8 + FMT_E5M2: return launch_mb<A_BF16, FMT_E5M2>(p, tmap, MB, ls, stream);
+    case A_S8 * 8 + FMT_E4M3_REF: return launch_mb<A_S8, FMT_E4M3_REF>(p, tmap, MB, ls, stream);
+    case A_S8 * 8 + FMT_E5M2: return launch_mb<A_S8, FMT_E5M2>(p, tmap, MB, ls, stream);
+    case A_S8 * 8 + FMT_E4M3FN: return launch_mb<A_S8, FMT_E4M3FN>(p, tmap, MB, ls, stream);
+    case A_S8 * 8 + FMT_NATIVE_E5M2: return launch_mb<A_S8, FMT_NATIVE_E5M2>(p, tmap, MB, ls, stream);
+    case A_F16 * 8 + FMT_WGT: return launch_mb<A_F16, FMT_WGT>(p, tmap, MB, ls, stream);
     default: return cudaErrorInvalidValue;
   }
 }
+
+void gemv_set_stream_k(int mode) { g_stream_k.store(mode); }
 
 unsigned int gemv_device_error(bool clear) {
   unsigned int v = 0;

@@ -96,6 +96,7 @@ extern "C" int fp8imma_gemm_rowquant_noalloc(const fp8imma_gemm_args* a, void* s
   p.out_row_major = a->out_layout;
   const bool fast = a->K > 0 && (a->K % 16) == 0 && (reinterpret_cast<uintptr_t>(a->A) & 15u) == 0 &&
                     (reinterpret_cast<uintptr_t>(a->B) & 15u) == 0;
+  p.no_alloc = 1;  // stream-K only when its scratch already exists
   if (fast) return (int)launch_gemv_s8(p, a->a_type, a->b_format, 0, st);
   return (int)launch_generic_s8(p, a->a_type, a->b_format, st);
 }

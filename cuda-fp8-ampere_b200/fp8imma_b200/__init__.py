@@ -40,6 +40,7 @@ EXT_SYMBOLS = [
     "fp8imma_gemm_allgather",
     "fp8imma_fp8wgt_linear_forward",
     "fp8imma_set_splitk",
+    "fp8imma_set_stream_k",
     "fp8imma_set_small_m_max",
     "fp8imma_last_path",
     "fp8imma_set_pdl",
@@ -91,6 +92,8 @@ def lib() -> ctypes.CDLL:
     L.fp8imma_fp8wgt_linear_forward.argtypes = [P, P, F, P, I, I, I, P]
     L.fp8imma_set_splitk.restype = I
     L.fp8imma_set_splitk.argtypes = [I]
+    L.fp8imma_set_stream_k.restype = I
+    L.fp8imma_set_stream_k.argtypes = [I]
     L.fp8imma_set_small_m_max.restype = I
     L.fp8imma_set_small_m_max.argtypes = [I]
     L.fp8imma_set_tc_pair.restype = I

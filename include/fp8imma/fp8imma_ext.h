@@ -112,6 +112,13 @@ int fp8imma_gemm_allgather(const fp8imma_gemm_args* args, void* const* peer_out,
 // Tuning / introspection (no reference counterpart).
 // Force the K split of the small-M kernel (0 = automatic; 1, 2, 4 or 8).
 int fp8imma_set_splitk(int splits);
+// Small-M kernel form when no split is forced. Stream-K: persistent CTAs
+// with an even share of the weight bytes each, partial sums in a per-device
+// scratch ring allocated on first use. Clusters: K slices of a column tile
+// reducing in distributed shared memory. 1 (default) = stream-K where the
+// cluster form would need more than one wave of CTAs, else clusters;
+// 2 = always stream-K; 0 = always clusters.
+int fp8imma_set_stream_k(int mode);
 // Largest M routed to the small-M split-K kernel (default 64).
 int fp8imma_set_small_m_max(int m);
 // Large-M tensor-core kernel: 1 (default) = CTA-pair kernel (tcgen05
