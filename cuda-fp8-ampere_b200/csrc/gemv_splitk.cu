@@ -351,7 +351,7 @@ __device__ __forceinline__ void store_out(const GemvParams& p, int n, int m, int
 }
 
 template <int AT, int MB, int FMT>
-__global__ void __launch_bounds__(kThreads, 3)
+__global__ void __launch_bounds__(kThreads, 2)
     gemv_s8_splitk_kernel(const __grid_constant__ GemvParams p, const __grid_constant__ CUtensorMap tmap) {
   constexpr int MR = MB * 8;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
