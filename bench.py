@@ -199,6 +199,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-lib", action="store_true")
     ap.add_argument("--points", action="store_true", help="also time the other decode/70B shapes")
+    ap.add_argument("--points-only", default="", help="comma-separated subset of the --points shapes")
     ap.add_argument("--pdl", action="store_true", help="launch with programmatic dependent launch")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="N>1: in-kernel NVLink gather (peer) or NCCL all-gather")
@@ -397,7 +398,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_ref_lib:
         extra["ref_lib_b200"] = time_reference_lib(A, Bs, s16, M, Nl, K, gs, ainv, args.steps, copies)
     if rank == 0 and world == 1 and args.points:
-        extra["points"] = time_points(ext, args.steps)
+        extra["points"] = time_points(ext, args.steps, [x for x in args.points_only.split(",") if x])
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -467,19 +468,25 @@ def time_reference_lib(A, Bs, s16, M, N, K, gs, ainv, steps, copies):
             "timing": "eager launches, CUDA events"}
 
 
-def time_points(ext, steps):
-    """Other benchmark shapes, both paths: decode and 70B-style (split-K
+def time_points(ext, steps, only=None):
+    """Other benchmark shapes, all paths (int8-exact, native FP8, and the
+    fp8wgt linear where M is a multiple of 16): decode and 70B-style (split-K
     kernels), prefill / square / 70B M=4096 (tcgen05). CUDA-graph timed,
     weights rotated over > 2x L2 where they would fit in it."""
     import torch
 
+    import fp8imma_b200 as F
     from fp8imma_b200 import workloads as WL
+
+    wgt = F.wgt_ext()
 
     shapes = {"decode_m1": (1, 4096, 4096), "decode_m4": (4, 4096, 4096), "decode_m16": (16, 4096, 4096),
               "up70b_m1": (1, 28672, 8192), "up70b_m32": (32, 28672, 8192), "prefill": (2048, 11008, 4096),
               "square4096": (4096, 4096, 4096), "square8192": (8192, 8192, 8192), "up70b_m4096": (4096, 28672, 8192)}
     out = {}
     for name, (M, N, K) in shapes.items():
+        if only and name not in only:
+            continue
         w = WL.CONFIGS.get(name, {})
         B, s16, sig = WL.make_weights(N, K, w.get("sigma_w", 0.02), "e4m3", seed=0)
         A = WL.make_activations(M, K, w.get("dist", "normal"), w.get("outlier_frac", 0.0), seed=1)
@@ -488,9 +495,11 @@ def time_points(ext, steps):
         Bs = [B] + [B.clone() for _ in range(copies - 1)]
         D = torch.empty(N, M, dtype=torch.float16, device=A.device)
         n = min(steps, 200) if M <= 64 else 10
-        for path in ("int8", "fp8"):
+        for path in ("int8", "fp8", "fp8wgt") if M % 16 == 0 else ("int8", "fp8"):
             def call(i):
-                if path == "int8":
+                if path == "fp8wgt":
+                    wgt.fp8_linear_forward(A, Bs[i % copies], 0.05)
+                elif path == "int8":
                     ext.imma_fp8_gemm(A, Bs[i % copies], s16, None, 1.0 / 16, 16.0, "tensor", "e4m3", "int8",
                                       "float16", "col", False, D)
                 else:
@@ -512,10 +521,12 @@ def time_points(ext, steps):
             ev1.record()
             torch.cuda.synchronize()
             ms = ev0.elapsed_time(ev1) / n
+            nbytes = alg_bytes(M, N, K) + (2 * M * N if path == "fp8wgt" else 0)  # fp32 output
             out["%s_%s" % (name, path)] = {"us": round(ms * 1e3, 3),
-                                          "GB/s": round(alg_bytes(M, N, K) / (ms * 1e-3) / 1e9, 1),
-                                          "TFLOPS": round(2 * M * N * K / (ms * 1e-3) / 1e12, 3),
-                                          "kernel_path": ext.last_path()}
+                                          "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                                          "TFLOPS": round(2 * M * N * K / (ms * 1e-3) / 1e12, 3)}
+            if path != "fp8wgt":
+                out["%s_%s" % (name, path)]["kernel_path"] = ext.last_path()
             del g
         ref = time_reference_lib(A, [B], s16, M, N, K, 1.0 / 16, 16.0, 3 if M > 64 else 50, 1)
         if "ms_per_call" in ref:

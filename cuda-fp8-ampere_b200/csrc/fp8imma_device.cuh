@@ -150,15 +150,28 @@ __device__ __forceinline__ uint32_t fast_scale(uint16_t inv_h) {
   return (uint32_t)v | ((uint32_t)v << 16);
 }
 
-// f16x2 pair holding 1536 + p in each half -> saturated int8 in the low byte
-// of each half: 1536 + p rounds p to the nearest integer (ties to even; the
-// ulp of fp16 in [1024, 2048) is 1 and 1536 is even), and clamping the fp16
-// bit pattern as a signed 16-bit integer to [1536-128, 1536+127] saturates,
-// with +Inf / -Inf / negative sums landing on the correct end.
+__device__ __forceinline__ uint32_t hmin2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("min.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t hmax2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Two f16x2 products -> four saturated int8 = sat_rni(p), packed. Products
+// here are never NaN (killed codes are finite, scales are finite
+// and non-zero on the fast paths): clamp in fp16 to [-128, 127] first
+// (rounding the clamped value equals clamping the rounded one for every
+// finite or infinite p), then 1536 + p rounds to the nearest integer (ties to
+// even: the fp16 ulp in [1024, 2048) is 1 and 1536 is even), whose low byte
+// is the int8 result.
 __device__ __forceinline__ uint32_t round_sat_pack(uint32_t p01, uint32_t p23) {
-  const uint32_t kMagic = 0x66006600u, kLo = 0x65806580u, kHi = 0x667F667Fu;
-  uint32_t r01 = min_s16x2(max_s16x2(hadd2_rn(p01, kMagic), kLo), kHi);
-  uint32_t r23 = min_s16x2(max_s16x2(hadd2_rn(p23, kMagic), kLo), kHi);
+  const uint32_t kMagic = 0x66006600u, kLo = 0xD800D800u, kHi = 0x57F057F0u;  // 1536, -128, 127
+  uint32_t r01 = hadd2_rn(hmin2(hmax2(p01, kLo), kHi), kMagic);
+  uint32_t r23 = hadd2_rn(hmin2(hmax2(p23, kLo), kHi), kMagic);
   return prmt(r01, r23, 0x6420u);
 }
 
