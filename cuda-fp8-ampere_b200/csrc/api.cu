@@ -9,6 +9,7 @@
 #include "fp8imma/imma_fp8.h"
 #include "fp8imma_kernels.h"
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 #include <set>
@@ -193,6 +194,42 @@ static cudaError_t gemm_ex(const fp8imma_gemm_args* a, cudaStream_t stream) {
   return run_int8(p, a->a_type, a->b_format, group, stream);
 }
 
+// Small host<->device transfers for fp8imma_gemm_host_io. A kernel that
+// reads (or writes) page-locked host memory through its mapped device
+// address moves a few hundred KB in a couple of microseconds and keeps the
+// whole step on the compute engine; a copy-engine transfer of the same size
+// costs several microseconds of engine switch and DMA set-up on each side of
+// the GEMM. Pageable host memory is not device-accessible and goes through
+// cudaMemcpyAsync.
+__global__ void __launch_bounds__(256) copy16_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src,
+                                                     size_t n16) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+
+static const void* mapped_host_ptr(const void* p) {
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged) return p;
+  if (attr.type == cudaMemoryTypeHost && attr.devicePointer) return attr.devicePointer;
+  return nullptr;  // pageable host memory
+}
+
+static cudaError_t copy_via_sm(void* dst, const void* src, size_t bytes, cudaStream_t st) {
+  const void* d = mapped_host_ptr(dst);
+  const void* s = mapped_host_ptr(src);
+  const bool vec = d && s && ((reinterpret_cast<uintptr_t>(d) | reinterpret_cast<uintptr_t>(s) | bytes) & 15u) == 0;
+  if (!vec) return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, st);
+  const size_t n16 = bytes >> 4;
+  const int grid = (int)std::min<size_t>((n16 + 255) / 256, 296);
+  if (grid > 0)
+    copy16_kernel<<<grid, 256, 0, st>>>(static_cast<uint4*>(const_cast<void*>(d)), static_cast<const uint4*>(s), n16);
+  return cudaGetLastError();
+}
+
 }  // namespace fp8imma_b200
 
 using namespace fp8imma_b200;
@@ -303,6 +340,19 @@ int fp8imma_launch_imma_fp8_actquant_v4_bf16(int kChunk, const void* A, const vo
 
 int fp8imma_gemm(const fp8imma_gemm_args* args, void* stream) {
   return (int)gemm_ex(args, static_cast<cudaStream_t>(stream));
+}
+
+int fp8imma_gemm_host_io(const fp8imma_gemm_args* a, const void* A_host, void* D_host, void* stream) {
+  if (!a || !A_host || !D_host || !a->A || !a->D || a->M <= 0 || a->N <= 0 || a->K <= 0)
+    return (int)cudaErrorInvalidValue;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t a_bytes = (size_t)a->M * a->K * (a->a_type == FP8IMMA_A_S8 ? 1 : 2);
+  const size_t d_bytes = (size_t)a->M * a->N * 2;
+  cudaError_t e = copy_via_sm(const_cast<void*>(a->A), A_host, a_bytes, st);
+  if (e != cudaSuccess) return (int)e;
+  int r = fp8imma_gemm(a, stream);
+  if (r != 0) return r;
+  return (int)copy_via_sm(D_host, a->D, d_bytes, st);
 }
 
 int fp8imma_set_splitk(int splits) {

@@ -36,6 +36,7 @@ REF_SYMBOLS = [
 ]
 EXT_SYMBOLS = [
     "fp8imma_gemm",
+    "fp8imma_gemm_host_io",
     "fp8imma_gemm_rowquant_noalloc",
     "fp8imma_gemm_allgather",
     "fp8imma_fp8wgt_linear_forward",
@@ -84,6 +85,8 @@ def lib() -> ctypes.CDLL:
         f.argtypes = [I, P, P, P, P, I, I, I, F, F, P]
     L.fp8imma_gemm.restype = I
     L.fp8imma_gemm.argtypes = [ctypes.POINTER(FP8ImmaGemmArgs), P]
+    L.fp8imma_gemm_host_io.restype = I
+    L.fp8imma_gemm_host_io.argtypes = [ctypes.POINTER(FP8ImmaGemmArgs), P, P, P]
     L.fp8imma_gemm_allgather.restype = I
     L.fp8imma_gemm_allgather.argtypes = [ctypes.POINTER(FP8ImmaGemmArgs), P, P, I, I, ctypes.c_uint, P]
     L.fp8imma_gemm_rowquant_noalloc.restype = I

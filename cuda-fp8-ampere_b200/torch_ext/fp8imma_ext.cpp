@@ -74,7 +74,8 @@ std::vector<torch::Tensor> imma_fp8_gemm(torch::Tensor A, torch::Tensor B, c10::
                                          c10::optional<torch::Tensor> col_scales_f32, double global_scale,
                                          double a_inv_scale, std::string act_quant, std::string b_format,
                                          std::string path, std::string out_dtype, std::string out_layout,
-                                         bool return_acc, c10::optional<torch::Tensor> out) {
+                                         bool return_acc, c10::optional<torch::Tensor> out,
+                                         c10::optional<torch::Tensor> a_host, c10::optional<torch::Tensor> out_host) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda(), "A and B must be CUDA tensors");
   TORCH_CHECK(A.is_contiguous() && B.is_contiguous(), "A and B must be contiguous");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2, "A must be [M,K] and B [N,K]");
@@ -137,7 +138,21 @@ std::vector<torch::Tensor> imma_fp8_gemm(torch::Tensor A, torch::Tensor B, c10::
   a.global_scale = (float)global_scale;
   a.a_inv_scale = (float)a_inv_scale;
   a.D = D.data_ptr();
-  check_launch(fp8imma_gemm(&a, (void*)at::cuda::getCurrentCUDAStream()), "fp8imma_gemm");
+  void* stream = (void*)at::cuda::getCurrentCUDAStream();
+  if (a_host.has_value() || out_host.has_value()) {
+    // host-side activations in, host-side result out (fp8imma_gemm_host_io):
+    // A is refreshed from a_host and D is copied to out_host on this stream
+    TORCH_CHECK(a_host.has_value() && out_host.has_value(), "a_host and out_host go together");
+    auto& ah = *a_host;
+    auto& dh = *out_host;
+    TORCH_CHECK(!ah.is_cuda() && ah.is_contiguous() && ah.scalar_type() == A.scalar_type() && ah.sizes() == A.sizes(),
+                "a_host must be a contiguous host tensor shaped and typed like A");
+    TORCH_CHECK(!dh.is_cuda() && dh.is_contiguous() && dh.scalar_type() == odt && dh.sizes() == at::IntArrayRef(shape),
+                "out_host must be a contiguous host tensor shaped and typed like the output");
+    check_launch(fp8imma_gemm_host_io(&a, ah.data_ptr(), dh.data_ptr(), stream), "fp8imma_gemm_host_io");
+  } else {
+    check_launch(fp8imma_gemm(&a, stream), "fp8imma_gemm");
+  }
   return {D, acc.defined() ? acc : torch::Tensor()};
 }
 
@@ -156,7 +171,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("col_scales_f16") = py::none(), py::arg("col_scales_f32") = py::none(), py::arg("global_scale") = 1.0,
         py::arg("a_inv_scale") = 1.0, py::arg("act_quant") = "tensor", py::arg("b_format") = "e4m3",
         py::arg("path") = "int8", py::arg("out_dtype") = "float16", py::arg("out_layout") = "col",
-        py::arg("return_acc") = false, py::arg("out") = py::none());
+        py::arg("return_acc") = false, py::arg("out") = py::none(), py::arg("a_host") = py::none(),
+        py::arg("out_host") = py::none());
   m.def("last_path", &last_path, "kernel family of the last call on this thread");
   m.def("set_splitk", &set_splitk, "force the small-M K split (0 = automatic)");
   m.def("set_small_m_max", &set_small_m_max, "largest M for the small-M kernel");

@@ -61,6 +61,14 @@ typedef struct fp8imma_gemm_args {
 // buffers (cudaMallocAsync on `stream`).
 int fp8imma_gemm(const fp8imma_gemm_args* args, void* stream);
 
+// fp8imma_gemm with host-side activations and result: copies A_host (M x K
+// elements of the activation type; page-locked memory for an asynchronous
+// copy) into args->A, runs fp8imma_gemm, and copies args->D (M x N outputs)
+// back into D_host, all queued on `stream` (the call returns before the
+// copies finish; synchronise the stream before reading D_host). args->A and
+// args->D are the caller's device staging buffers.
+int fp8imma_gemm_host_io(const fp8imma_gemm_args* args, const void* A_host, void* D_host, void* stream);
+
 // Largest M accepted by fp8imma_gemm_rowquant_noalloc.
 #define FP8IMMA_NOALLOC_MAX_M 4096
 

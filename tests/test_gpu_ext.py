@@ -154,3 +154,32 @@ def test_fp8linear_module(cuda):
     out = mod(A)
     C_o = O.fp8wgt(A.cpu().numpy().view(np.uint16), B.cpu().numpy(), 0.1)
     assert np.abs(out.cpu().numpy() - C_o).max() / np.abs(C_o).max() < 1e-3
+
+
+@pytest.mark.parametrize("M,N,K,pinned", [(16, 4096, 1024, True), (3, 200, 528, True), (256, 512, 512, True),
+                                          (16, 256, 512, False), (5, 130, 96, False)])
+def test_host_io_entry_matches_device_entry(cuda, M, N, K, pinned):
+    """fp8imma_gemm_host_io: host activations in, host result out, on the
+    caller's stream; bit-identical to fp8imma_gemm on device buffers. Pinned
+    host memory is moved by a kernel through its mapped address, pageable
+    memory by the copy engine."""
+    e = F.ext()
+    A, B, s, _ = inputs(M, N, K, seed=M + 5)
+    dA = torch.from_numpy(A.view(np.int16)).cuda().view(torch.float16)
+    dB, ds = torch.from_numpy(B).cuda(), torch.from_numpy(s.view(np.int16)).cuda()
+    D_ref, _ = e.imma_fp8_gemm(dA, dB, ds, None, 0.5, 8.0, "tensor", "e4m3", "int8", "float16", "col", False, None)
+    a_host = torch.from_numpy(A.view(np.int16)).view(torch.float16).clone()
+    d_host = torch.full((N, M), float("nan"), dtype=torch.float16)
+    if pinned:
+        a_host, d_host = a_host.pin_memory(), d_host.pin_memory()
+    a_stage = torch.zeros(M, K, dtype=torch.float16, device="cuda")
+    d_stage = torch.empty(N, M, dtype=torch.float16, device="cuda")
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        e.imma_fp8_gemm(a_stage, dB, ds, None, 0.5, 8.0, "tensor", "e4m3", "int8", "float16", "col", False, d_stage,
+                        a_host=a_host, out_host=d_host)
+    st.synchronize()
+    assert torch.equal(d_host.view(torch.int16), D_ref.cpu().view(torch.int16))
+    with pytest.raises(RuntimeError, match="go together"):
+        e.imma_fp8_gemm(a_stage, dB, ds, None, 0.5, 8.0, "tensor", "e4m3", "int8", "float16", "col", False, d_stage,
+                        a_host=a_host)
