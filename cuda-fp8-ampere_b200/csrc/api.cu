@@ -375,6 +375,12 @@ int fp8imma_set_small_m_max(int m) {
 
 int fp8imma_last_path(void) { return t_last_path; }
 
+int fp8imma_set_tc_splitk(int splits) {
+  if (splits < -1 || splits == 0 || splits > 64) return (int)cudaErrorInvalidValue;
+  tc_set_splitk(splits);
+  return 0;
+}
+
 int fp8imma_set_tc_pair(int enable) {
   tc_set_pair_mode(enable != 0);
   return 0;

@@ -66,7 +66,12 @@ cudaError_t launch_gemm_tc_fp8(const void* A, int a_type, const uint8_t* B, int 
 unsigned int tc_device_error(bool clear);
 cudaError_t launch_gemm_tc_wgt(const void* A_f16, const uint8_t* B, float scale_b, float* C, int M, int N, int K,
                                void* scratch, cudaStream_t stream);
-void tc_set_pair_mode(bool on);  // tcgen05 GEMM: CTA-pair (cta_group::2) kernel or 1-CTA kernel
+void tc_set_pair_mode(bool on);
+// CTA-pair kernel K splits: -1 automatic (default), else forced.
+void tc_set_splitk(int splits);
+int tc_pick_splits(int M, int N, int Kbytes);
+// split-K accumulator workspace the CTA-pair kernel needs for this shape
+size_t tc_splitk_ws_bytes(int M, int N, int Kbytes);  // tcgen05 GEMM: CTA-pair (cta_group::2) kernel or 1-CTA kernel
 cudaError_t launch_quant_a_e4m3(const void* A, int a_type, int M, int K, uint8_t* Aq, float* row_scale,
                                 cudaStream_t stream);
 

@@ -23,6 +23,8 @@
 #include "fp8imma_kernels.h"
 #include "sm100_async.cuh"
 
+#include <algorithm>
+
 using namespace fp8imma_dev;
 
 namespace fp8imma_b200 {
@@ -123,6 +125,9 @@ struct TcParams {
   void* D;
   int32_t* acc_out;
   int out_bf16, out_row_major;
+  int splits;          // CTA-pair kernel: K splits per tile (1 = none)
+  int kb_per_split;    // 128-byte K blocks per split
+  uint32_t* ws;        // splits > 1: raw accumulators [split][n][m] (int32 or fp32 bits)
 };
 
 template <int KIND>
@@ -336,31 +341,32 @@ __global__ void __launch_bounds__(256) quant_a_s8_kernel(const void* __restrict_
   }
 }
 
-// FP8 weights -> int8 with the reference chain. One thread handles 64 bytes
-// of one weight row (amortising the per-column inverse scale). K % 16 == 0.
+// FP8 weights -> int8 with the reference chain. One warp per weight row at a
+// time (the column's inverse scale is formed once per row), each lane
+// transcoding 16 contiguous bytes of every 512-byte step, two steps in
+// flight. K % 16 == 0.
 template <int FMT>
 __global__ void __launch_bounds__(256) transcode_b_kernel(const uint8_t* __restrict__ B, int N, int K,
                                                           const uint16_t* __restrict__ scale_u16,
                                                           unsigned long long scale_tex, int8_t* __restrict__ Bq) {
-  const int chunks = (K + 63) >> 6;
-  const size_t total = (size_t)N * chunks;
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    const int n = (int)(i / chunks);
-    const int k0 = (int)(i - (size_t)n * chunks) << 6;
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  const int k16 = K >> 4;  // 16-byte vectors per row
+  for (int n = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); n < N; n += warps) {
     const uint16_t sb = scale_tex ? tex1Dfetch<unsigned short>((cudaTextureObject_t)scale_tex, n) : scale_u16[n];
     const uint16_t inv = inv_scale_bits(sb);
     const bool fast = fast_ok<FMT>(inv);
     const uint32_t fs = fast_scale<FMT>(inv);
-    const uint4* src = reinterpret_cast<const uint4*>(B + (size_t)n * K + k0);
-    uint4* dst = reinterpret_cast<uint4*>(Bq + (size_t)n * K + k0);
-    const int nv = min(4, (K - k0) >> 4);
-    uint4 v[4];
+    const uint4* src = reinterpret_cast<const uint4*>(B + (size_t)n * K);
+    uint4* dst = reinterpret_cast<uint4*>(Bq + (size_t)n * K);
+    for (int v0 = lane; v0 < k16; v0 += 64) {
+      uint4 v[2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      if (j < nv) v[j] = ldg_stream_v4(src + j);
+      for (int j = 0; j < 2; ++j)
+        if (v0 + 32 * j < k16) v[j] = ldg_stream_v4(src + v0 + 32 * j);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (j < nv) {
+      for (int j = 0; j < 2; ++j) {
+        if (v0 + 32 * j >= k16) continue;
         uint4 o;
         if (fast) {
           if (FMT == FMT_E5M2) {
@@ -380,7 +386,7 @@ __global__ void __launch_bounds__(256) transcode_b_kernel(const uint8_t* __restr
           o.z = transcode4_exact<FMT>(v[j].z, inv);
           o.w = transcode4_exact<FMT>(v[j].w, inv);
         }
-        dst[j] = o;
+        dst[v0 + 32 * j] = o;
       }
     }
   }
@@ -524,6 +530,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   const uint32_t rank = cluster_ctarank();  // 0 = leader (issues the MMAs)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int ntiles = p.tiles_w * p.tiles_x;  // tiles of 256 x 256
+  const int nwork = ntiles * p.splits;       // (tile, K split) work items
   const int nkb = (p.K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -559,9 +566,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = pair; tile < ntiles && ok; tile += npairs) {
+      for (int wi = pair; wi < nwork && ok; wi += npairs) {
+        const int tile = wi / p.splits, split = wi - tile * p.splits;
         const int tw = tile % p.tiles_w, tx = tile / p.tiles_w;
-        for (int kb = 0; kb < nkb; ++kb) {
+        const int kb0 = split * p.kb_per_split, kb1 = min(nkb, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY))) break;
           uint8_t* sw = smem + stage * kStageBytes2;
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes2);
@@ -589,19 +598,21 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       uint32_t phase = 0;
       bool ok = true;
       int it = 0;
-      for (int tile = pair; tile < ntiles && ok; tile += npairs, ++it) {
+      for (int wi = pair; wi < nwork && ok; wi += npairs, ++it) {
         const int buf = it & 1;
+        const int split = wi % p.splits;
+        const int kb0 = split * p.kb_per_split, kb1 = min(nkb, kb0 + p.kb_per_split);
         if (!(ok = mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1u, ERR_WAIT_TMEM_EMPTY))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * 256);
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!(ok = mbar_wait(&full[stage], phase, ERR_WAIT_FULL))) break;
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * kStageBytes2);
           const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + kHalfBytes);
 #pragma unroll
           for (int j = 0; j < kBK / 32; ++j)
-            umma2<KIND>(d_tmem, adesc + 2 * j, bdesc + 2 * j, p.idesc, (kb | j) != 0);
+            umma2<KIND>(d_tmem, adesc + 2 * j, bdesc + 2 * j, p.idesc, (kb != kb0) || (j != 0));
           umma2_commit(&empty[stage], 0x3);
           if (++stage == kStages2) {
             stage = 0;
@@ -617,8 +628,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     // ---- epilogue (both CTAs): this CTA's 128 TMEM lanes = 128 weight columns
     const int q = warp & 3;
     int it = 0;
-    for (int tile = pair; tile < ntiles; tile += npairs, ++it) {
+    for (int wi = pair; wi < nwork; wi += npairs, ++it) {
       const int buf = it & 1;
+      const int tile = wi / p.splits, split = wi - tile * p.splits;
       const int tw = tile % p.tiles_w, tx = tile / p.tiles_w;
       if (!mbar_wait(&tfull[buf], (it >> 1) & 1, ERR_WAIT_TMEM_FULL)) break;
       tc_fence_after();
@@ -638,6 +650,18 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         tmem_ld32(taddr + j0, r);
         const int mbase = tx * 256 + j0;
         if (!nok || mbase >= p.M) continue;
+        if (p.splits > 1) {  // raw accumulators of this K split; tc_splitk_reduce_kernel finishes
+          uint32_t* dst = p.ws + ((size_t)split * p.N + n) * p.M + mbase;
+          const int mc = min(32, p.M - mbase);
+          if (mc == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
+#pragma unroll
+            for (int v4 = 0; v4 < 8; ++v4)
+              reinterpret_cast<uint4*>(dst)[v4] = make_uint4(r[4 * v4], r[4 * v4 + 1], r[4 * v4 + 2], r[4 * v4 + 3]);
+          } else {
+            for (int j = 0; j < mc; ++j) dst[j] = r[j];
+          }
+          continue;
+        }
         if (KIND == KIND_F16) {  // fp8wgt: fp32 accumulators straight to row-major C[m, n]
           float* C = static_cast<float*>(p.D);
           const int mc = min(32, p.M - mbase);
@@ -706,6 +730,70 @@ __host__ __device__ constexpr uint32_t make_idesc2(int a_fmt) {
 }
 
 bool g_use_pair = true;
+int g_tc_splitk = -1;  // -1 automatic, else forced K splits of the CTA-pair kernel
+
+// Split-K finish: sum the raw accumulators of the K splits in a fixed order
+// (exact for int32; deterministic for fp32) and apply the same epilogue as
+// the tensor-core kernel. 32 x 32 (n, m) tiles through shared memory so that
+// both the column-major reads and a row-major store are coalesced.
+template <int KIND>
+__global__ void __launch_bounds__(256) tc_splitk_reduce_kernel(const TcParams p) {
+  __shared__ float tile[32][33];
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  const int m0 = blockIdx.x * 32, n0 = blockIdx.y * 32;
+  const size_t plane = (size_t)p.N * p.M;
+  const bool row_out = KIND == KIND_F16 || p.out_row_major;
+  // all four rows' partials of a split are loaded before any is added
+  int32_t si4[4] = {0, 0, 0, 0};
+  float sf4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const int m = m0 + tx;
+  for (int s = 0; s < p.splits; ++s) {
+    uint32_t x[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int n = n0 + ty + 8 * i;
+      x[i] = (n < p.N && m < p.M) ? __ldcs(p.ws + (size_t)s * plane + (size_t)n * p.M + m) : 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (KIND == KIND_I8) si4[i] += (int32_t)x[i];
+      else sf4[i] += __uint_as_float(x[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int n = n0 + ty + 8 * i;
+    float v = 0.0f;
+    if (n < p.N && m < p.M) {
+      const size_t e = (size_t)n * p.M + m;
+      const int32_t si = si4[i];
+      const float sf = sf4[i];
+      if (KIND == KIND_F16) {
+        v = sf;
+      } else if (KIND == KIND_I8) {
+        uint16_t sb = p.scale_tex ? tex1Dfetch<unsigned short>((cudaTextureObject_t)p.scale_tex, n) : p.scale_u16[n];
+        float se = __half2float(__ushort_as_half(sb)) * (p.row_g ? p.row_g[m] : p.global_scale);
+        if (p.col_scale_f32) se = se * p.col_scale_f32[n];
+        v = (float)si * se;
+        if (p.acc_out) p.acc_out[e] = si;
+      } else {
+        v = sf * (p.row_g ? p.row_g[m] : 1.0f) * (p.col_scale_f32 ? p.col_scale_f32[n] : 1.0f);
+      }
+      if (!row_out) static_cast<uint16_t*>(p.D)[e] = store_val(v, p.out_bf16);
+    }
+    tile[ty + 8 * i][tx] = v;
+  }
+  if (!row_out) return;
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty + 8 * i, n = n0 + tx;
+    if (n >= p.N || m >= p.M) continue;
+    const float v = tile[tx][ty + 8 * i];
+    if (KIND == KIND_F16) static_cast<float*>(p.D)[(size_t)m * p.N + n] = v;
+    else static_cast<uint16_t*>(p.D)[(size_t)m * p.N + n] = store_val(v, p.out_bf16);
+  }
+}
 
 template <int KIND>
 cudaError_t launch_tc2(TcParams p, const void* W, const void* X, int a_fmt, cudaStream_t stream) {
@@ -721,7 +809,13 @@ cudaError_t launch_tc2(TcParams p, const void* W, const void* X, int a_fmt, cuda
   if ((e = ensure_smem_attr((const void*)kern, smem)) != cudaSuccess) return e;
   const int ntiles = p.tiles_w * p.tiles_x;
   const int maxpairs = num_sms_current() / 2;
-  const int pairs = ntiles < maxpairs ? ntiles : maxpairs;
+  const int nkb = (p.K + kBK - 1) / kBK;
+  if (!p.ws) p.splits = 1;
+  if (p.splits < 1) p.splits = 1;
+  p.kb_per_split = (nkb + p.splits - 1) / p.splits;
+  p.splits = (nkb + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
+  const int nwork = ntiles * p.splits;
+  const int pairs = nwork < maxpairs ? nwork : maxpairs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(kThreadsTC, 1, 1);
@@ -734,7 +828,10 @@ cudaError_t launch_tc2(TcParams p, const void* W, const void* X, int a_fmt, cuda
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, p, mw, mx);
+  if ((e = cudaLaunchKernelEx(&cfg, kern, p, mw, mx)) != cudaSuccess || p.splits == 1) return e;
+  const dim3 rgrid((p.M + 31) / 32, (p.N + 31) / 32);
+  tc_splitk_reduce_kernel<KIND><<<rgrid, dim3(32, 8), 0, stream>>>(p);
+  return cudaGetLastError();
 }
 
 int grid_for(size_t work_items) {
@@ -770,11 +867,37 @@ unsigned int tc_device_error(bool clear) {
   return v;
 }
 
-size_t gemm_tc_scratch_bytes(int M, int N, int K, bool native) {
+void tc_set_splitk(int splits) { g_tc_splitk = splits; }
+
+// K splits for the CTA-pair kernel: enough (tile, split) work items to give
+// most CTA pairs one, at least 4 K blocks (512 bytes of K) per split, and only
+// where that is 3 or more splits.
+int tc_pick_splits(int M, int N, int Kbytes) {
+  if (!g_use_pair) return 1;
+  const int nkb = (Kbytes + kBK - 1) / kBK;
+  if (g_tc_splitk >= 1) return g_tc_splitk < nkb ? g_tc_splitk : nkb;
+  const int ntiles = ((N + 255) / 256) * ((M + 255) / 256);
+  const int pairs = num_sms_current() / 2;
+  int s = pairs / ntiles;
+  if (s > 8) s = 8;
+  if (s > nkb / 4) s = nkb / 4;
+  return s < 3 ? 1 : s;  // two splits measured no faster than none (the finishing pass costs ~4 us)
+}
+
+size_t tc_splitk_ws_bytes(int M, int N, int Kbytes) {
+  const int s = tc_pick_splits(M, N, Kbytes);
+  return s > 1 ? (((size_t)s * N * M * 4 + 255) & ~size_t(255)) : 0;
+}
+
+static size_t tc_ws_offset(int M, int N, int K, bool native) {
   size_t a = ((size_t)M * K + 255) & ~size_t(255);
   size_t b = native ? 0 : (((size_t)N * K + 255) & ~size_t(255));
   size_t r = native ? (((size_t)M * 4 + 255) & ~size_t(255)) : 0;
   return a + b + r;
+}
+
+size_t gemm_tc_scratch_bytes(int M, int N, int K, bool native) {
+  return tc_ws_offset(M, N, K, native) + tc_splitk_ws_bytes(M, N, K);
 }
 
 // int8-exact large-M GEMM: prep (A quant, B transcode) into `scratch`, then tcgen05.
@@ -792,10 +915,10 @@ cudaError_t launch_gemm_tc_s8(const GemvParams& gp, int a_type, int fmt, void* s
       default: quant_a_s8_kernel<A_S8><<<grid, 256, 0, stream>>>(gp.A, M, K, gp.a_inv_h, gp.row_inv_h, Aq); break;
     }
   }
-  // 2. weights
+  // 2. weights: one warp per row, at most 8 resident CTAs of 8 warps per SM
   {
-    const size_t items = (size_t)N * ((K + 63) >> 6);
-    const int grid = grid_for(items);
+    const int sms = num_sms_current();
+    const int grid = std::min((N + 7) / 8, sms * 8);
     if (fmt == FMT_E5M2)
       transcode_b_kernel<FMT_E5M2><<<grid, 256, 0, stream>>>(gp.B, N, K, gp.scale_u16, gp.scale_tex, Bq);
     else
@@ -823,7 +946,11 @@ cudaError_t launch_gemm_tc_s8(const GemvParams& gp, int a_type, int fmt, void* s
   p.acc_out = gp.acc_out;
   p.out_bf16 = gp.out_bf16;
   p.out_row_major = gp.out_row_major;
-  if (g_use_pair) return launch_tc2<KIND_I8>(p, Bq, Aq, 0, stream);
+  if (g_use_pair) {
+    p.splits = tc_pick_splits(M, N, K);
+    p.ws = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(scratch) + tc_ws_offset(M, N, K, false));
+    return launch_tc2<KIND_I8>(p, Bq, Aq, 0, stream);
+  }
   return launch_tc<KIND_I8>(p, mw, mx, stream);
 }
 
@@ -862,30 +989,28 @@ cudaError_t launch_gemm_tc_fp8(const void* A, int a_type, const uint8_t* B, int 
   p.D = D;
   p.out_bf16 = out_bf16;
   p.out_row_major = out_row_major;
-  if (g_use_pair) return launch_tc2<KIND_F8>(p, B, Aq, b_fmt == 1 ? 1 : 0, stream);
+  if (g_use_pair) {
+    p.splits = tc_pick_splits(M, N, K);
+    p.ws = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(scratch) + tc_ws_offset(M, N, K, true));
+    return launch_tc2<KIND_F8>(p, B, Aq, b_fmt == 1 ? 1 : 0, stream);
+  }
   return launch_tc<KIND_F8>(p, mw, mx, stream);
 }
 
 namespace {
 // fp8wgt weights -> fp16 (torch_ext/fp8wgt/fp8wgt_ext_cuda.cu:195-198):
-// fp16_rn(float(lut_e4m3[b]) * scale_b), 16 bytes in, 32 bytes out per step.
+// fp16_rn(float(lut_e4m3[b]) * scale_b), 16 bytes in, 32 bytes out per step;
+// sb is scale_b / 256 for the packed decode (wgt_decode4_fast).
 __global__ void __launch_bounds__(256) decode_b_f16_kernel(const uint8_t* __restrict__ B, size_t n16, float sb,
-                                                           uint16_t* __restrict__ Bh) {
+                                                           int fast, uint16_t* __restrict__ Bh) {
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x) {
     const uint4 v = ldg_stream_v4(reinterpret_cast<const uint4*>(B) + i);
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
     uint32_t o[8];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t b0 = (w[j] >> (16 * h)) & 0xFFu, b1 = (w[j] >> (16 * h + 8)) & 0xFFu;
-        const float f0 = __fmul_rn(__half2float(__ushort_as_half(ref_e4m3_bits(b0))), sb);
-        const float f1 = __fmul_rn(__half2float(__ushort_as_half(ref_e4m3_bits(b1))), sb);
-        uint32_t r;
-        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(f1), "f"(f0));
-        o[2 * j + h] = r;
-      }
+      if (fast) wgt_decode4_fast(w[j], sb, o[2 * j], o[2 * j + 1]);
+      else wgt_decode4_exact(w[j], sb, o[2 * j], o[2 * j + 1]);
     }
     uint4* dst = reinterpret_cast<uint4*>(Bh) + 2 * i;
     dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
@@ -902,7 +1027,10 @@ cudaError_t launch_gemm_tc_wgt(const void* A_f16, const uint8_t* B, float scale_
   uint16_t* Bh = static_cast<uint16_t*>(scratch);
   const size_t n16 = (size_t)N * K / 16;
   const int sms = num_sms_current();
-  decode_b_f16_kernel<<<sms * 8, 256, 0, stream>>>(B, n16, scale_b, Bh);
+  // packed decode with scale/256 unless that is an fp32 subnormal (then the scalar one)
+  const float mag = scale_b < 0.0f ? -scale_b : scale_b;
+  const int fast = (mag == 0.0f || !(mag < 0x1p-117f)) ? 1 : 0;
+  decode_b_f16_kernel<<<sms * 8, 256, 0, stream>>>(B, n16, fast ? scale_b * 0.00390625f : scale_b, fast, Bh);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   TcParams p = {};
@@ -910,6 +1038,8 @@ cudaError_t launch_gemm_tc_wgt(const void* A_f16, const uint8_t* B, float scale_
   p.N = N;
   p.K = 2 * K;  // the pipeline works in bytes of K
   p.D = C;
+  p.splits = tc_pick_splits(M, N, 2 * K);
+  p.ws = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(scratch) + (((size_t)N * K * 2 + 255) & ~size_t(255)));
   return launch_tc2<KIND_F16>(p, Bh, A_f16, 0, stream);
 }
 

@@ -132,6 +132,11 @@ int fp8imma_set_small_m_max(int m);
 // Large-M tensor-core kernel: 1 (default) = CTA-pair kernel (tcgen05
 // cta_group::2, 256x256 tiles), 0 = single-CTA kernel (128x256 tiles).
 int fp8imma_set_tc_pair(int enable);
+// K splits of the CTA-pair tcgen05 kernel: -1 (default) = automatic (split
+// when the 256 x 256 tiles would leave most CTA pairs idle, e.g. M <= 512 at
+// N = 4096), 1 = never, n > 1 = forced. Partial accumulators go to
+// stream-ordered scratch and a second kernel finishes the epilogue.
+int fp8imma_set_tc_splitk(int splits);
 // Programmatic dependent launch (default off). When on, a GEMM may start
 // streaming its weights and reading its column scales while the previous
 // kernel in the stream is still running; activations are read, and outputs
