@@ -202,8 +202,9 @@ def main():
     ap.add_argument("--points", action="store_true", help="also time the other decode/70B shapes")
     ap.add_argument("--points-only", default="", help="comma-separated subset of the --points shapes")
     ap.add_argument("--pdl", action="store_true", help="launch with programmatic dependent launch")
-    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
-                    help="N>1: in-kernel NVLink gather (peer) or NCCL all-gather")
+    ap.add_argument("--gather", default="peer", choices=["peer", "peer-epilogue", "nccl"],
+                    help="N>1: NVLink gather in a kernel after the GEMM (peer), in the GEMM's epilogue "
+                         "(peer-epilogue), or NCCL all-gather")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     w = WORKLOADS[args.workload]
@@ -240,7 +241,8 @@ def main():
     gs, ainv = 1.0 / 16.0, 16.0
 
     fused = None
-    if world > 1 and args.gather == "peer" and M <= 64:
+    F.lib().fp8imma_set_fused_gather(1 if args.gather == "peer-epilogue" else 0)
+    if world > 1 and args.gather in ("peer", "peer-epilogue") and M <= 64:
         from fp8imma_b200.sharded import FusedGatherFP8Gemm
 
         fused = FusedGatherFP8Gemm(B, s16, M)
@@ -288,7 +290,8 @@ def main():
         torch.cuda.synchronize()
         barrier()
     if world > 1:
-        timing += ", in-kernel NVLink gather + flag barrier" if fused is not None else ", NCCL all-gather in step"
+        timing += ((", NVLink gather in the GEMM epilogue + flag barrier" if args.gather == "peer-epilogue" else
+                    ", NVLink gather kernel + flag barrier") if fused is not None else ", NCCL all-gather in step")
     sampler = ClockSampler(local)
     sampler.start()
     # keep the GPU busy ~0.6 s so the clock samples reflect the loaded state

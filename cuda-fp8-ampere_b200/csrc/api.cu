@@ -41,7 +41,11 @@ cudaError_t ensure_smem_attr(const void* kernel, int bytes) {
   std::lock_guard<std::mutex> lk(mu);
   auto key = std::make_pair(kernel, dev);
   if (done.count(key)) return cudaSuccess;
-  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaFuncAttributes fa;
+  e = cudaFuncGetAttributes(&fa, kernel);
+  if (e != cudaSuccess) return e;
+  // the opt-in limit counts static shared memory too
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - (int)fa.sharedSizeBytes);
   if (e == cudaSuccess) done.insert(key);
   return e;
 }

@@ -35,8 +35,20 @@ struct GemvParams {
   float wgt_scale;                  // FMT_WGT: scale_b (or scale_b / 256 when wgt_fast)
   int wgt_fast;                     // FMT_WGT: packed decode allowed for this scale
   int no_alloc;                     // the launcher may not allocate device memory
+  // column-parallel gather fused into the split-K epilogue (world > 1)
+  int world, rank;
+  unsigned int epoch;                       // 0: counted on the device
+  unsigned long long peer_rows[8];          // this rank's output slice inside each rank's full output
+  unsigned long long peer_sig[8];           // each rank's signal pad (u32 counters, epoch at kPeerEpochSlot)
   unsigned long long* trace;        // FP8IMMA_TRACE builds only: per-CTA phase timestamps
 };
+
+// Signal pad layout (u32 words): [0, 8) arrival counters of the separate
+// gather kernel, [8, 16) arrival counters of the gather fused into the GEMM
+// epilogue, 32 / 33 the two forms' call epochs. 64 words in all.
+constexpr int kPeerEpochSlot = 32;
+constexpr int kPeerFusedSlot = 8;
+constexpr int kPeerFusedEpochSlot = 33;
 
 cudaError_t ensure_smem_attr(const void* kernel, int bytes);
 

@@ -350,6 +350,80 @@ __device__ __forceinline__ void store_out(const GemvParams& p, int n, int m, int
   }
 }
 
+// Column-parallel output gather fused into the epilogue (world > 1): the
+// CTA's finished outputs (columns [n_lo, n_hi), rows [m0, m0+MR) of this
+// rank's slice, already stored locally) are copied into the same place of
+// every peer's full output with 16-byte stores over NVLink, then published
+// with one system-scope release increment of this rank's counter in each
+// peer's signal pad (slots kPeerFusedSlot + rank). The first CTA of the grid
+// then advances this rank's call epoch (slot kPeerFusedEpochSlot of its own
+// pad) and waits (bounded) until every peer's counter in its own pad has
+// reached epoch x (CTAs per grid): all peers' slices have landed.
+__device__ __forceinline__ void peer_publish(const GemvParams& p, int n_lo, int n_hi, int m0, int MR,
+                                             unsigned int* target_s) {
+  __syncthreads();  // this CTA's local output stores are done
+  const int m1 = min(p.M, m0 + MR);
+  if (n_lo < n_hi && m0 < m1) {
+    const uint8_t* src = static_cast<const uint8_t*>(p.D);
+    if (m0 == 0 && m1 == p.M) {  // one contiguous run of the col-major slice
+      const size_t b0 = (size_t)n_lo * p.M * 2, nb = (size_t)(n_hi - n_lo) * p.M * 2;
+      for (int q = 0; q < p.world; ++q) {
+        if (q == p.rank) continue;
+        uint8_t* dst = reinterpret_cast<uint8_t*>(p.peer_rows[q]);
+        if (((reinterpret_cast<uintptr_t>(src + b0) | reinterpret_cast<uintptr_t>(dst + b0) | nb) & 15u) == 0) {
+          for (size_t i = threadIdx.x; i < (nb >> 4); i += blockDim.x)
+            reinterpret_cast<uint4*>(dst + b0)[i] = reinterpret_cast<const uint4*>(src + b0)[i];
+        } else {
+          for (size_t i = threadIdx.x; i < (nb >> 1); i += blockDim.x)
+            reinterpret_cast<uint16_t*>(dst + b0)[i] = reinterpret_cast<const uint16_t*>(src + b0)[i];
+        }
+      }
+    } else {  // per-column runs of m1 - m0 rows
+      const int rows = m1 - m0, cnt = (n_hi - n_lo) * rows;
+      for (int q = 0; q < p.world; ++q) {
+        if (q == p.rank) continue;
+        uint16_t* dst = reinterpret_cast<uint16_t*>(p.peer_rows[q]);
+        for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
+          const int c = i / rows, r = i - c * rows;
+          const size_t off = (size_t)(n_lo + c) * p.M + m0 + r;
+          dst[off] = reinterpret_cast<const uint16_t*>(src)[off];
+        }
+      }
+    }
+  }
+  __syncthreads();  // every copy of this CTA is issued before the release below
+  if ((int)threadIdx.x < p.world && (int)threadIdx.x != p.rank) {
+    unsigned int* slot = reinterpret_cast<unsigned int*>(p.peer_sig[threadIdx.x]) + kPeerFusedSlot + p.rank;
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(slot) : "memory");
+  }
+  if (blockIdx.x != 0 || blockIdx.y != 0 || blockIdx.z != 0) return;
+  if (threadIdx.x == 0) {
+    unsigned int e = p.epoch;
+    if (e == 0) {  // epoch counted on the device: advances on every launch, graph replays included
+      unsigned int* ctr = reinterpret_cast<unsigned int*>(p.peer_sig[p.rank]) + kPeerFusedEpochSlot;
+      e = *ctr + 1;
+      *ctr = e;
+    }
+    *target_s = e * (gridDim.x * gridDim.y * gridDim.z);
+  }
+  __syncthreads();
+  const unsigned int target = *target_s;
+  if ((int)threadIdx.x < p.world && (int)threadIdx.x != p.rank) {
+    const unsigned int* mine = reinterpret_cast<const unsigned int*>(p.peer_sig[p.rank]) + kPeerFusedSlot + threadIdx.x;
+    const unsigned long long t0 = globaltimer_ns();
+    for (;;) {
+      unsigned int v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if ((int)(v - target) >= 0) break;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicCAS(&g_fp8imma_device_error, 0u, ERR_WAIT_PEER);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
 template <int AT, int MB, int FMT>
 __global__ void __launch_bounds__(kThreads, 2)
     gemv_s8_splitk_kernel(const __grid_constant__ GemvParams p, const __grid_constant__ CUtensorMap tmap) {
@@ -526,6 +600,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
   if (threadIdx.x == 0) TRACE_POINT(p, 7);
+  if (p.world > 1)
+    peer_publish(p, tile_n0 + rank * cols_per, min(p.N, tile_n0 + (rank + 1) * cols_per), m0, MR,
+                 reinterpret_cast<unsigned int*>(smem + kBarOffset + 128));
   cluster.sync();  // keep shared memory alive until every peer has read it
   if (threadIdx.x == 0) TRACE_POINT(p, 8);
 }
@@ -931,7 +1008,7 @@ cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaSt
   // projections, where the cluster form's 2-per-SM waves are uneven
   const long long all_units = (long long)mchunks * tiles * ((p.K + 63) / 64);
   const bool big = all_units >= (long long)kSkAutoUnits * 2 * sms;
-  if (splits == 0 && g_stream_k.load() && (g_stream_k.load() == 2 || big) &&
+  if (splits == 0 && p.world <= 1 && g_stream_k.load() && (g_stream_k.load() == 2 || big) &&
       (long long)tiles * mchunks <= kSkMaxCounters) {
     const long long units = (long long)mchunks * tiles * ((p.K + 63) / 64);
     // at least kSkMinUnits halves (48 KB of weights) per CTA keeps tiles to a few contributors

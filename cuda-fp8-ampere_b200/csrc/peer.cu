@@ -18,8 +18,9 @@ namespace fp8imma_b200 {
 namespace {
 
 static __device__ unsigned int g_peer_error;
+bool g_fused_gather = false;  // gather in the GEMM epilogue (else, default, a separate gather kernel)
 constexpr unsigned long long kPeerWaitNs = 2000000000ull;
-constexpr int kEpochSlot = 32;  // per-rank call counter (device-side epoch) in each rank's own pad
+constexpr int kEpochSlot = kPeerEpochSlot;  // per-rank call counter (device-side epoch) in each rank's own pad
 constexpr int kGatherBlocks = 32;
 constexpr int kGatherThreads = 256;
 
@@ -30,18 +31,30 @@ struct Ptrs8 {
 __global__ void __launch_bounds__(kGatherThreads) peer_gather_kernel(Ptrs8 outs, Ptrs8 pads, int world, int rank,
                                                                      unsigned long long byte0, unsigned long long nbytes,
                                                                      unsigned int epoch_arg) {
-  // 1. copy this rank's rows to every peer (16-byte granules, grid-strided)
+  // 1. copy this rank's rows to every peer (grid-strided). byte0 = rank * N *
+  //    M * 2 is only as aligned as N * M allows, so 16-byte granules are used
+  //    only when both addresses are 16-byte aligned (all ranks' buffers share
+  //    one alignment), else 4- or 2-byte ones.
   const uint8_t* src = reinterpret_cast<const uint8_t*>(outs.p[rank]) + byte0;
-  const unsigned long long n16 = nbytes >> 4;
+  const unsigned long long tid = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const unsigned long long nthr = (unsigned long long)gridDim.x * blockDim.x;
   for (int r = 1; r < world; ++r) {
     const int peer = (rank + r) % world;  // stagger destinations across ranks
     uint8_t* dst = reinterpret_cast<uint8_t*>(outs.p[peer]) + byte0;
-    for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < n16;
-         i += (unsigned long long)gridDim.x * blockDim.x)
-      reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
-    for (unsigned long long i = (n16 << 4) + (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < nbytes;
-         i += (unsigned long long)gridDim.x * blockDim.x)
-      dst[i] = src[i];
+    const uintptr_t al = reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst);
+    unsigned long long done = 0;
+    if ((al & 15u) == 0) {
+      const unsigned long long n16 = nbytes >> 4;
+      for (unsigned long long i = tid; i < n16; i += nthr)
+        reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+      done = n16 << 4;
+    } else if ((al & 3u) == 0) {
+      const unsigned long long n4 = nbytes >> 2;
+      for (unsigned long long i = tid; i < n4; i += nthr)
+        reinterpret_cast<uint32_t*>(dst)[i] = reinterpret_cast<const uint32_t*>(src)[i];
+      done = n4 << 2;
+    }
+    for (unsigned long long i = done + tid; i < nbytes; i += nthr) dst[i] = src[i];
   }
   __syncthreads();
   // 2. publish: one release increment per peer (cumulative over this CTA's
@@ -111,6 +124,12 @@ unsigned int peer_device_error(bool clear) {
 
 using namespace fp8imma_b200;
 
+extern "C" int fp8imma_set_fused_gather(int enable) {
+  if (enable != 0 && enable != 1) return (int)cudaErrorInvalidValue;
+  g_fused_gather = enable != 0;
+  return 0;
+}
+
 extern "C" int fp8imma_gemm_allgather(const fp8imma_gemm_args* a, void* const* peer_out, void* const* peer_signal,
                                       int world, int rank, unsigned int epoch, void* stream) {
   if (!a || !peer_out || !peer_signal || world < 1 || world > 8 || rank < 0 || rank >= world)
@@ -144,6 +163,18 @@ extern "C" int fp8imma_gemm_allgather(const fp8imma_gemm_args* a, void* const* p
   p.a_inv_h = __half_as_ushort(__float2half(a->a_inv_scale));
   p.out_bf16 = a->out_type;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (world > 1 && g_fused_gather) {
+    // the split-K kernel's epilogue writes into every peer's output and
+    // signals; its first CTA waits for the peers (no separate gather kernel)
+    p.world = world;
+    p.rank = rank;
+    p.epoch = epoch;
+    for (int r = 0; r < world; ++r) {
+      p.peer_rows[r] = outs[r] + (unsigned long long)rank * a->N * a->M * 2;
+      p.peer_sig[r] = pads[r];
+    }
+    return (int)launch_gemv_s8(p, a->a_type, a->b_format, 0, st);
+  }
   cudaError_t e = launch_gemv_s8(p, a->a_type, a->b_format, 0, st);
   if (e != cudaSuccess) return (int)e;
   if (world == 1) return 0;

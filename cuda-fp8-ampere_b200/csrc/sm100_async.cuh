@@ -20,6 +20,7 @@ enum : unsigned int {
   ERR_WAIT_EMPTY = 2u,
   ERR_WAIT_TMEM_FULL = 3u,
   ERR_WAIT_TMEM_EMPTY = 4u,
+  ERR_WAIT_PEER = 5u,  // a peer GPU's gather signal did not arrive
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any healthy wait

@@ -39,6 +39,7 @@ EXT_SYMBOLS = [
     "fp8imma_gemm_host_io",
     "fp8imma_gemm_rowquant_noalloc",
     "fp8imma_gemm_allgather",
+    "fp8imma_set_fused_gather",
     "fp8imma_fp8wgt_linear_forward",
     "fp8imma_set_splitk",
     "fp8imma_set_stream_k",
@@ -89,6 +90,8 @@ def lib() -> ctypes.CDLL:
     L.fp8imma_gemm_host_io.restype = I
     L.fp8imma_gemm_host_io.argtypes = [ctypes.POINTER(FP8ImmaGemmArgs), P, P, P]
     L.fp8imma_gemm_allgather.restype = I
+    L.fp8imma_set_fused_gather.restype = I
+    L.fp8imma_set_fused_gather.argtypes = [I]
     L.fp8imma_gemm_allgather.argtypes = [ctypes.POINTER(FP8ImmaGemmArgs), P, P, I, I, ctypes.c_uint, P]
     L.fp8imma_gemm_rowquant_noalloc.restype = I
     L.fp8imma_gemm_rowquant_noalloc.argtypes = [ctypes.POINTER(FP8ImmaGemmArgs), P]

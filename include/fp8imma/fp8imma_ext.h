@@ -102,13 +102,14 @@ int fp8imma_fp8wgt_linear_forward(const void* A_f16, const void* B_u8, float sca
 // (<= 8) passes its weight shard (args->B, [N_shard, K]) and shard scales;
 // the GEMM writes this rank's [N_shard, M] slice of the col-major output into
 // rows rank*N_shard.. of its own full buffer peer_out[rank] ([world*N_shard,
-// M]), then a gather kernel copies the slice into every peer's buffer over
-// NVLink (peer stores) and waits until every rank's slice has arrived here.
-// peer_out / peer_signal hold device pointers to all ranks' buffers, valid in
-// this process (e.g. a symmetric allocation); each signal pad needs `world`
-// zero-initialised uint32 slots; `epoch` must grow by one per call (1, 2, ...),
-// or be 0: the epoch is then counted on the device in slot 32 of this rank's
-// own pad (pads need 33 slots), so a captured CUDA graph can be replayed.
+// M]) and into the same rows of every peer's buffer over NVLink (peer
+// stores, from the GEMM's epilogue or a gather kernel, see
+// fp8imma_set_fused_gather), then waits until every rank's slice has arrived
+// here. peer_out / peer_signal hold device pointers to all ranks' buffers,
+// valid in this process (e.g. a symmetric allocation); each signal pad needs
+// 64 zero-initialised uint32 slots; `epoch` must grow by one per call
+// (1, 2, ...), or be 0: the epoch is then counted on the device in the pad
+// of this rank, so a captured CUDA graph can be replayed.
 // Int8-exact path, per-tensor quantisation, col-major output, small M (the
 // split-K kernel). The call returns when the launches are queued; the output
 // is complete on every rank once this stream reaches the end of the call.
@@ -116,6 +117,13 @@ int fp8imma_fp8wgt_linear_forward(const void* A_f16, const void* B_u8, float sca
 // reading from the previous call (alternate two buffers).
 int fp8imma_gemm_allgather(const fp8imma_gemm_args* args, void* const* peer_out, void* const* peer_signal, int world,
                            int rank, unsigned int epoch, void* stream);
+// 1: the gather of fp8imma_gemm_allgather runs in the GEMM's own epilogue
+// (peer stores + one system-scope release per CTA, first CTA waits for the
+// peers); 0 (default, measured faster: 17.3 vs 19.4 us per decode step on 2
+// GPUs): a separate gather kernel after the GEMM. Each form keeps its own
+// counters and epoch in the signal pad, so the setting may change between
+// calls.
+int fp8imma_set_fused_gather(int enable);
 
 // Tuning / introspection (no reference counterpart).
 // Force the K split of the small-M kernel (0 = automatic; 1, 2, 4 or 8).

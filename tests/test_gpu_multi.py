@@ -46,17 +46,23 @@ def _worker(rank, world, port, M, N, K, q):
             from fp8imma_b200.sharded import FusedGatherFP8Gemm
 
             fused = FusedGatherFP8Gemm(inp.B[n0:n1], inp.scales_u16[n0:n1], M)
-            for _ in range(3):
-                Df = fused(inp.A, 1.0 / 16, 16.0)
-                torch.cuda.synchronize()
-                ok = ok and bool(torch.equal(Df.view(torch.int16), full.view(torch.int16)))
-            ok = ok and F.lib().fp8imma_device_error(0) == 0
+            L = F.lib()
+            # gather kernel, then in the GEMM epilogue, then the kernel again: each
+            # form keeps its own counters, so switching between calls is safe
+            for mode in (0, 1, 0):
+                assert L.fp8imma_set_fused_gather(mode) == 0
+                for _ in range(2):
+                    Df = fused(inp.A, 1.0 / 16, 16.0)
+                    torch.cuda.synchronize()
+                    ok = ok and bool(torch.equal(Df.view(torch.int16), full.view(torch.int16)))
+            L.fp8imma_set_fused_gather(0)
+            ok = ok and L.fp8imma_device_error(0) == 0
         q.put((rank, ok))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("M,N,K", [(16, 4096, 4096), (300, 2048, 1024)])
+@pytest.mark.parametrize("M,N,K", [(16, 4096, 4096), (37, 4004, 1024), (300, 2048, 1024)])
 def test_column_parallel_nccl_2gpu(cuda, M, N, K):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
