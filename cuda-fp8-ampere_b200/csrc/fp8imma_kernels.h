@@ -84,6 +84,8 @@ void tc_set_splitk(int splits);
 int tc_pick_splits(int M, int N, int Kbytes);
 // split-K accumulator workspace the CTA-pair kernel needs for this shape
 size_t tc_splitk_ws_bytes(int M, int N, int Kbytes);  // tcgen05 GEMM: CTA-pair (cta_group::2) kernel or 1-CTA kernel
+cudaError_t launch_quant_a_s8(const void* A, int a_type, int M, int K, uint16_t a_inv_h, const uint16_t* row_inv_h,
+                              int8_t* Aq, cudaStream_t stream);
 cudaError_t launch_quant_a_e4m3(const void* A, int a_type, int M, int K, uint8_t* Aq, float* row_scale,
                                 cudaStream_t stream);
 

@@ -954,6 +954,20 @@ cudaError_t launch_gemm_tc_s8(const GemvParams& gp, int a_type, int fmt, void* s
   return launch_tc<KIND_I8>(p, mw, mx, stream);
 }
 
+// Reference int8 activation quantisation alone (A_S8 copies). Used by the
+// small-M kernel when the same activations would otherwise be re-quantised by
+// many column tiles.
+cudaError_t launch_quant_a_s8(const void* A, int a_type, int M, int K, uint16_t a_inv_h, const uint16_t* row_inv_h,
+                              int8_t* Aq, cudaStream_t stream) {
+  const int grid = grid_for((size_t)M * (K >> 3));
+  switch (a_type) {
+    case A_F16: quant_a_s8_kernel<A_F16><<<grid, 256, 0, stream>>>(A, M, K, a_inv_h, row_inv_h, Aq); break;
+    case A_BF16: quant_a_s8_kernel<A_BF16><<<grid, 256, 0, stream>>>(A, M, K, a_inv_h, row_inv_h, Aq); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
 // Per-row E4M3 activation quantisation alone (small-M native path).
 cudaError_t launch_quant_a_e4m3(const void* A, int a_type, int M, int K, uint8_t* Aq, float* row_scale,
                                 cudaStream_t stream) {

@@ -993,13 +993,39 @@ int gemv_pick_splits(int N, int K, int mchunks, int num_sms) {
   return S;
 }
 
+static cudaError_t launch_gemv_impl(GemvParams p, int a_type, int fmt, int splits, cudaStream_t stream);
+
 cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaStream_t stream) {
+  // Every column tile stages and quantises its own copy of the activations;
+  // when that repeated work is large (many tiles, M >= 16) the activations are
+  // quantised once by a pre-pass and the kernel copies int8 rows instead.
+  const long long tiles = (p.N + kTileN - 1) / kTileN;
+  if (!p.no_alloc && (fmt == FMT_E4M3_REF || fmt == FMT_E5M2) && (a_type == A_F16 || a_type == A_BF16) &&
+      p.M >= 16 && (long long)p.M * p.K * tiles >= (16LL << 20) && p.keff_a == p.K) {
+    void* aq = nullptr;
+    cudaError_t e = cudaMallocAsync(&aq, (size_t)p.M * p.K, stream);
+    if (e != cudaSuccess) return e;
+    e = launch_quant_a_s8(p.A, a_type, p.M, p.K, p.a_inv_h, p.row_inv_h, static_cast<int8_t*>(aq), stream);
+    if (e == cudaSuccess) {
+      GemvParams q = p;
+      q.A = aq;
+      e = launch_gemv_impl(q, A_S8, fmt, splits, stream);
+    }
+    cudaError_t e2 = cudaFreeAsync(aq, stream);
+    return e != cudaSuccess ? e : e2;
+  }
+  return launch_gemv_impl(p, a_type, fmt, splits, stream);
+}
+
+static cudaError_t launch_gemv_impl(GemvParams p, int a_type, int fmt, int splits, cudaStream_t stream) {
   if (fmt == FMT_E4M3FN || fmt == FMT_NATIVE_E5M2) a_type = A_S8;  // pre-quantised E4M3 activations are copied
   const int MB = p.M >= 32 ? 4 : (p.M + 7) / 8;
   const int MR = MB * 8;
   const int mchunks = (p.M + MR - 1) / MR;
   const int tiles = (p.N + kTileN - 1) / kTileN;
-  const int kc_max = MR > 16 ? 512 : 1024;
+  // activation chunk staged per refill: 1024 K (fp16 rows at 32 rows: 512, to
+  // keep two CTAs' shared memory within an SM)
+  const int kc_max = (MR > 16 && fmt == FMT_WGT) ? 512 : 1024;
   LaunchShape ls = {};
   ls.mchunks = mchunks;
   const int sms = num_sms_current();

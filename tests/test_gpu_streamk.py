@@ -22,8 +22,9 @@ from test_gpu_ext import inputs
 
 pytestmark = pytest.mark.gpu
 
+# (32, 8192, 8192): M*K*tiles >= 16M, so activations are quantised once by a pre-pass
 SHAPES = [(1, 128, 64), (3, 200, 528), (16, 4096, 4096), (37, 300, 1040), (64, 1000, 8192), (8, 28672, 1024),
-          (33, 130, 1088), (2, 8192, 16384)]
+          (33, 130, 1088), (2, 8192, 16384), (32, 8192, 8192)]
 
 
 @pytest.fixture(params=[2, 0], ids=["streamk", "cluster"])
@@ -54,7 +55,7 @@ def test_int8_bitexact_both_forms(sk_mode, M, N, K):
     assert bits_equal(to_np_bits(D), D_o).all()
 
 
-@pytest.mark.parametrize("M,N,K", [(5, 384, 2112), (48, 640, 640)])
+@pytest.mark.parametrize("M,N,K", [(5, 384, 2112), (48, 640, 640), (48, 8192, 6144)])
 def test_int8_row_quant_bf16_both_forms(sk_mode, M, N, K):
     A, B, s, sig, D, acc = run_int8(M, N, K, seed=7, row_quant=True, a_bf16=True)
     D_o, acc_o = O.gemm_ex(A, B, s, a_bf16=True, row_quant=True, col_scale_f32=sig, global_scale=0.05,
