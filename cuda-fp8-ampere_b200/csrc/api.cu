@@ -385,6 +385,12 @@ int fp8imma_set_tc_splitk(int splits) {
   return 0;
 }
 
+int fp8imma_set_tc_tile_x(int rows) {
+  if (rows != 0 && rows != 128 && rows != 192 && rows != 256) return (int)cudaErrorInvalidValue;
+  tc_set_tile_x(rows);
+  return 0;
+}
+
 int fp8imma_set_tc_pair(int enable) {
   tc_set_pair_mode(enable != 0);
   return 0;

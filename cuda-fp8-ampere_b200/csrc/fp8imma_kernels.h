@@ -81,6 +81,8 @@ cudaError_t launch_gemm_tc_wgt(const void* A_f16, const uint8_t* B, float scale_
 void tc_set_pair_mode(bool on);
 // CTA-pair kernel K splits: -1 automatic (default), else forced.
 void tc_set_splitk(int splits);
+// CTA-pair kernel activation rows per tile: 0 automatic (default), or 256 / 192 / 128.
+void tc_set_tile_x(int rows);
 int tc_pick_splits(int M, int N, int Kbytes);
 // split-K accumulator workspace the CTA-pair kernel needs for this shape
 size_t tc_splitk_ws_bytes(int M, int N, int Kbytes);  // tcgen05 GEMM: CTA-pair (cta_group::2) kernel or 1-CTA kernel

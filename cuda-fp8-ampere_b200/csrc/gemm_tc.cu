@@ -125,6 +125,7 @@ struct TcParams {
   void* D;
   int32_t* acc_out;
   int out_bf16, out_row_major;
+  int tile_x;          // CTA-pair kernel: activation rows per tile (256, 192 or 128; MMA N)
   int splits;          // CTA-pair kernel: K splits per tile (1 = none)
   int kb_per_split;    // 128-byte K blocks per split
   uint32_t* ws;        // splits > 1: raw accumulators [split][n][m] (int32 or fp32 bits)
@@ -529,7 +530,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();  // 0 = leader (issues the MMAs)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int ntiles = p.tiles_w * p.tiles_x;  // tiles of 256 x 256
+  const int ntiles = p.tiles_w * p.tiles_x;  // tiles of 256 weight columns x tile_x activation rows
   const int nwork = ntiles * p.splits;       // (tile, K split) work items
   const int nkb = (p.K + kBK - 1) / kBK;
 
@@ -573,10 +574,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY))) break;
           uint8_t* sw = smem + stage * kStageBytes2;
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes2);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (kHalfBytes + (p.tile_x >> 1) * kBK));
           const uint32_t fb = full_leader + stage * 8;
           tma_load_2d_pair(sw, &mapW, fb, kb * kBK, tw * 256 + 128 * (int)rank);
-          tma_load_2d_pair(sw + kHalfBytes, &mapX, fb, kb * kBK, tx * 256 + 128 * (int)rank);
+          tma_load_2d_pair(sw + kHalfBytes, &mapX, fb, kb * kBK, tx * p.tile_x + (p.tile_x >> 1) * (int)rank);
           if (++stage == kStages2) {
             stage = 0;
             phase ^= 1u;
@@ -645,10 +646,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
       uint16_t* D = static_cast<uint16_t*>(p.D);
 #pragma unroll 1
-      for (int j0 = 0; j0 < 256; j0 += 32) {
+      for (int j0 = 0; j0 < p.tile_x; j0 += 32) {
         uint32_t r[32];
         tmem_ld32(taddr + j0, r);
-        const int mbase = tx * 256 + j0;
+        const int mbase = tx * p.tile_x + j0;
         if (!nok || mbase >= p.M) continue;
         if (p.splits > 1) {  // raw accumulators of this K split; tc_splitk_reduce_kernel finishes
           uint32_t* dst = p.ws + ((size_t)split * p.N + n) * p.M + mbase;
@@ -722,15 +723,42 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 
 // M=256 instruction descriptor for the pair MMA
 template <int KIND>
-__host__ __device__ constexpr uint32_t make_idesc2(int a_fmt) {
-  // kind::f16 (fp16 x fp16, fp32 accumulate): a/b format 0 = F16
+__host__ __device__ constexpr uint32_t make_idesc2(int a_fmt, int n) {
+  // kind::f16 (fp16 x fp16, fp32 accumulate): a/b format 0 = F16; M = 256, N = n
   return (KIND == KIND_I8 ? (2u << 4) | (1u << 7) | (1u << 10)
                           : (1u << 4) | (KIND == KIND_F16 ? 0u : ((uint32_t)a_fmt << 7))) |
-         ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
 
 bool g_use_pair = true;
 int g_tc_splitk = -1;  // -1 automatic, else forced K splits of the CTA-pair kernel
+int g_tc_tile_x = 0;   // 0 automatic, else forced activation rows per tile (256, 192, 128)
+bool g_tc_tile_model = false;  // the rounds model below is kept for reference, not used
+
+// Activation rows per CTA-pair tile. Tiles are dealt round-robin to the CTA
+// pairs, so the last round can run mostly empty (4096^2: 256 tiles of 256 on
+// 74 pairs = 3.46 rounds). Narrower tiles balance the rounds but cost more
+// operand traffic per MAC; measured (4096^2, 2048x11008x4096, 8192^3,
+// 4096x28672x8192) 192 and 128 were 5-60% slower than 256 everywhere, so 256
+// is used unless forced. (Model: minimise rounds x (rows + 64).)
+int tc_pick_tile_x(int M, int N) {
+  if (g_tc_tile_x) return g_tc_tile_x;
+  if (!g_tc_tile_model) return 256;  // measured: narrower tiles were slower on every shape tried
+  const int pairs = num_sms_current() / 2;
+  const int tw = (N + 255) / 256;
+  int best = 256;
+  long long best_cost = -1;
+  for (int t : {256, 192, 128}) {
+    const long long tiles = (long long)tw * ((M + t - 1) / t);
+    const long long rounds = (tiles + pairs - 1) / pairs;
+    const long long cost = rounds * (t + 64);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = t;
+    }
+  }
+  return best;
+}
 
 // Split-K finish: sum the raw accumulators of the K splits in a fixed order
 // (exact for int32; deterministic for fp32) and apply the same epilogue as
@@ -800,10 +828,11 @@ cudaError_t launch_tc2(TcParams p, const void* W, const void* X, int a_fmt, cuda
   CUtensorMap mw, mx;
   cudaError_t e;
   if ((e = make_tmap_2d_u8(&mw, W, p.K, p.N, p.K, kBK, 128, true)) != cudaSuccess) return e;
-  if ((e = make_tmap_2d_u8(&mx, X, p.K, p.M, p.K, kBK, 128, true)) != cudaSuccess) return e;
+  p.tile_x = tc_pick_tile_x(p.M, p.N);
+  if ((e = make_tmap_2d_u8(&mx, X, p.K, p.M, p.K, kBK, p.tile_x / 2, true)) != cudaSuccess) return e;
   p.tiles_w = (p.N + 255) / 256;
-  p.tiles_x = (p.M + 255) / 256;
-  p.idesc = make_idesc2<KIND>(a_fmt);
+  p.tiles_x = (p.M + p.tile_x - 1) / p.tile_x;
+  p.idesc = make_idesc2<KIND>(a_fmt, p.tile_x);
   auto kern = gemm_tc2_kernel<KIND>;
   const int smem = kStages2 * kStageBytes2 + 1024 + 256;
   if ((e = ensure_smem_attr((const void*)kern, smem)) != cudaSuccess) return e;
@@ -868,6 +897,7 @@ unsigned int tc_device_error(bool clear) {
 }
 
 void tc_set_splitk(int splits) { g_tc_splitk = splits; }
+void tc_set_tile_x(int rows) { g_tc_tile_x = rows; }
 
 // K splits for the CTA-pair kernel: enough (tile, split) work items to give
 // most CTA pairs one, at least 4 K blocks (512 bytes of K) per split, and only
@@ -876,7 +906,8 @@ int tc_pick_splits(int M, int N, int Kbytes) {
   if (!g_use_pair) return 1;
   const int nkb = (Kbytes + kBK - 1) / kBK;
   if (g_tc_splitk >= 1) return g_tc_splitk < nkb ? g_tc_splitk : nkb;
-  const int ntiles = ((N + 255) / 256) * ((M + 255) / 256);
+  const int t = tc_pick_tile_x(M, N);
+  const int ntiles = ((N + 255) / 256) * ((M + t - 1) / t);
   const int pairs = num_sms_current() / 2;
   int s = pairs / ntiles;
   if (s > 8) s = 8;

@@ -145,6 +145,10 @@ int fp8imma_set_tc_pair(int enable);
 // N = 4096), 1 = never, n > 1 = forced. Partial accumulators go to
 // stream-ordered scratch and a second kernel finishes the epilogue.
 int fp8imma_set_tc_splitk(int splits);
+// Activation rows per CTA-pair tile (the MMA's N): 0 (default) = chosen per
+// shape to balance the rounds of tiles over the CTA pairs; 256, 192 or 128
+// forced.
+int fp8imma_set_tc_tile_x(int rows);
 // Programmatic dependent launch (default off). When on, a GEMM may start
 // streaming its weights and reading its column scales while the previous
 // kernel in the stream is still running; activations are read, and outputs

@@ -79,3 +79,51 @@ def test_splitk_setter_rejects_bad_values(cuda):
     assert L.fp8imma_set_tc_splitk(0) == 1
     assert L.fp8imma_set_tc_splitk(-2) == 1
     assert L.fp8imma_set_tc_splitk(-1) == 0
+
+
+@pytest.fixture(params=[192, 128, 0], ids=["x192", "x128", "auto"])
+def tile_x(request, cuda):
+    L = F.lib()
+    assert L.fp8imma_set_tc_pair(1) == 0
+    assert L.fp8imma_set_tc_tile_x(request.param) == 0
+    yield request.param
+    L.fp8imma_set_tc_tile_x(0)
+
+
+@pytest.mark.parametrize("M,N,K,out_row", [(300, 640, 1024, False), (1024, 512, 512, True), (97, 256, 2048, False)])
+def test_int8_tile_widths_bitexact(tile_x, M, N, K, out_row):
+    """Activation rows per CTA-pair tile (MMA N = 256 / 192 / 128): same
+    bits whatever the width, including ragged last tiles."""
+    e = F.ext()
+    A, B, s, sig = inputs(M, N, K, seed=M * 5 + N)
+    D_o, acc_o = O.gemm_ex(A, B, s, col_scale_f32=sig, global_scale=0.05, a_inv_scale=20.0, out_row_major=out_row,
+                           nthreads=16)
+    dA = torch.from_numpy(A.view(np.int16)).cuda().view(torch.float16)
+    D, acc = e.imma_fp8_gemm(dA, torch.from_numpy(B).cuda(), torch.from_numpy(s.view(np.int16)).cuda(),
+                             torch.from_numpy(sig).cuda(), 0.05, 20.0, "tensor", "e4m3", "int8", "float16",
+                             "row" if out_row else "col", True, None)
+    assert e.last_path() == 3
+    torch.cuda.synchronize()
+    assert (acc.cpu().numpy() == acc_o).all()
+    assert bits_equal(to_np_bits(D), D_o).all()
+
+
+def test_native_and_fp8wgt_tile_widths(tile_x):
+    e = F.ext()
+    M, N, K = 513, 384, 768
+    A, B, s, sig = inputs(M, N, K, seed=7)
+    D_o, _, _ = O.fp8_native(A, B, sig, b_fmt=O.FMT_E4M3FN)
+    dA = torch.from_numpy(A.view(np.int16)).cuda().view(torch.float16)
+    D, _ = e.imma_fp8_gemm(dA, torch.from_numpy(B).cuda(), None, torch.from_numpy(sig).cuda(), 1.0, 1.0, "row",
+                           "e4m3", "fp8", "float16", "col", False, None)
+    torch.cuda.synchronize()
+    got, ref = D.cpu().float().numpy(), D_o.view(np.float16).astype(np.float32)
+    assert np.abs(got - ref).max() <= 2e-3 * np.abs(ref).max() + 1e-6
+    rng = np.random.default_rng(3)
+    Aw = rng.standard_normal((256, 512)).astype(np.float16)
+    Bw = rng.integers(0, 0x78, (512, 512), dtype=np.uint8)
+    C_o = O.fp8wgt(Aw.view(np.uint16), Bw, 0.03, nthreads=16)
+    C = F.wgt_ext().fp8_linear_forward(torch.from_numpy(Aw).cuda(), torch.from_numpy(Bw).cuda(), 0.03)
+    torch.cuda.synchronize()
+    C = C.cpu().numpy()
+    assert np.abs(C - C_o).max() <= 1e-3 * np.abs(C_o).max()
