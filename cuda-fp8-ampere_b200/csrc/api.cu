@@ -150,6 +150,7 @@ static cudaError_t gemm_native(const fp8imma_gemm_args* a, cudaStream_t stream) 
       p.out_bf16 = a->out_type;
       p.out_row_major = a->out_layout;
       t_last_path = 5;
+      p.pdl = 1;  // weights stream while the quantisation kernel finishes; rows and scales are read after it
       e = launch_gemv_s8(p, A_S8, a->b_format == FP8IMMA_B_E5M2 ? 3 : 2, g_splitk.load(), stream);
     }
   } else {

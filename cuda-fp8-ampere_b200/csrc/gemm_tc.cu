@@ -318,6 +318,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 template <int AT>
 __global__ void __launch_bounds__(256) quant_a_s8_kernel(const void* __restrict__ A, int M, int K, uint16_t a_inv_h,
                                                          const uint16_t* __restrict__ row_inv_h, int8_t* __restrict__ Aq) {
+  // the GEMM that consumes these rows may be launched as a programmatic
+  // dependent: it starts streaming its weights now and waits for this grid
+  // (griddepcontrol.wait) before it reads the quantised rows
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const size_t total = (size_t)M * (K >> 3);
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const size_t e = i << 3;
@@ -399,6 +403,7 @@ __global__ void __launch_bounds__(256) transcode_b_kernel(const uint8_t* __restr
 template <int AT>
 __global__ void __launch_bounds__(256) quant_a_e4m3_kernel(const void* __restrict__ A, int M, int K,
                                                            uint8_t* __restrict__ Aq, float* __restrict__ row_scale) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // see quant_a_s8_kernel
   const int m = blockIdx.x;
   if (m >= M) return;
   const uint16_t* row = static_cast<const uint16_t*>(A) + (size_t)m * K;

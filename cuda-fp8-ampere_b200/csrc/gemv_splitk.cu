@@ -1009,6 +1009,7 @@ cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaSt
     if (e == cudaSuccess) {
       GemvParams q = p;
       q.A = aq;
+      q.pdl = 1;  // weights stream while the pre-pass finishes; activations are read after it
       e = launch_gemv_impl(q, A_S8, fmt, splits, stream);
     }
     cudaError_t e2 = cudaFreeAsync(aq, stream);
