@@ -392,6 +392,12 @@ int fp8imma_set_tc_tile_x(int rows) {
   return 0;
 }
 
+int fp8imma_set_tc_half_tail(int enable) {
+  if (enable != 0 && enable != 1) return (int)cudaErrorInvalidValue;
+  tc_set_half_tail(enable != 0);
+  return 0;
+}
+
 int fp8imma_set_tc_pair(int enable) {
   tc_set_pair_mode(enable != 0);
   return 0;

@@ -83,6 +83,8 @@ void tc_set_pair_mode(bool on);
 void tc_set_splitk(int splits);
 // CTA-pair kernel activation rows per tile: 0 automatic (default), or 256 / 192 / 128.
 void tc_set_tile_x(int rows);
+// CTA-pair kernel: last partial round of tiles as half-width items (default on).
+void tc_set_half_tail(bool on);
 int tc_pick_splits(int M, int N, int Kbytes);
 // split-K accumulator workspace the CTA-pair kernel needs for this shape
 size_t tc_splitk_ws_bytes(int M, int N, int Kbytes);  // tcgen05 GEMM: CTA-pair (cta_group::2) kernel or 1-CTA kernel

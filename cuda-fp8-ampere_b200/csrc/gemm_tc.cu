@@ -126,6 +126,8 @@ struct TcParams {
   int32_t* acc_out;
   int out_bf16, out_row_major;
   int tile_x;          // CTA-pair kernel: activation rows per tile (256, 192 or 128; MMA N)
+  int n_full;          // CTA-pair kernel: tiles run at full width; the rest run as two half-width items
+  uint32_t idesc_half; // instruction descriptor of the half-width items (N = tile_x / 2)
   int splits;          // CTA-pair kernel: K splits per tile (1 = none)
   int kb_per_split;    // 128-byte K blocks per split
   uint32_t* ws;        // splits > 1: raw accumulators [split][n][m] (int32 or fp32 bits)
@@ -520,10 +522,39 @@ __device__ __forceinline__ void umma2_commit(uint64_t* bar, uint16_t mask) {
       : "memory");
 }
 
+// Work item -> tile coordinates: tw (256-column weight tile), first activation
+// row x0, width xw (tile_x or tile_x / 2), K split.
+struct TcItem {
+  int tw, x0, xw, split;
+};
+__device__ __forceinline__ TcItem tc_item(const TcParams& p, int wi) {
+  TcItem it;
+  int tile;
+  if (p.splits > 1) {
+    tile = wi / p.splits;
+    it.split = wi - tile * p.splits;
+    it.xw = p.tile_x;
+    it.x0 = (tile / p.tiles_w) * p.tile_x;
+  } else if (wi < p.n_full) {
+    tile = wi;
+    it.split = 0;
+    it.xw = p.tile_x;
+    it.x0 = (tile / p.tiles_w) * p.tile_x;
+  } else {
+    const int j = wi - p.n_full;
+    tile = p.n_full + (j >> 1);
+    it.split = 0;
+    it.xw = p.tile_x >> 1;
+    it.x0 = (tile / p.tiles_w) * p.tile_x + (j & 1) * it.xw;
+  }
+  it.tw = tile % p.tiles_w;
+  return it;
+}
+
 template <int KIND>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     gemm_tc2_kernel(const __grid_constant__ TcParams p, const __grid_constant__ CUtensorMap mapW,
-                    const __grid_constant__ CUtensorMap mapX) {
+                    const __grid_constant__ CUtensorMap mapX, const __grid_constant__ CUtensorMap mapXh) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages2 * kStageBytes2);
@@ -536,7 +567,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   const uint32_t rank = cluster_ctarank();  // 0 = leader (issues the MMAs)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int ntiles = p.tiles_w * p.tiles_x;  // tiles of 256 weight columns x tile_x activation rows
-  const int nwork = ntiles * p.splits;       // (tile, K split) work items
+  // work items: (tile, K split); with splits == 1 the tiles past n_full (the
+  // last, partly empty round) run as two half-width items each, so that round
+  // spreads over twice as many CTA pairs
+  const int nwork = p.splits > 1 ? ntiles * p.splits : p.n_full + 2 * (ntiles - p.n_full);
   const int nkb = (p.K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -569,20 +603,21 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     if (lane == 0) {
       prefetch_tensormap(&mapW);
       prefetch_tensormap(&mapX);
+      prefetch_tensormap(&mapXh);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int wi = pair; wi < nwork && ok; wi += npairs) {
-        const int tile = wi / p.splits, split = wi - tile * p.splits;
-        const int tw = tile % p.tiles_w, tx = tile / p.tiles_w;
-        const int kb0 = split * p.kb_per_split, kb1 = min(nkb, kb0 + p.kb_per_split);
+        const TcItem it = tc_item(p, wi);
+        const int kb0 = it.split * p.kb_per_split, kb1 = min(nkb, kb0 + p.kb_per_split);
+        const CUtensorMap* mx = it.xw == p.tile_x ? &mapX : &mapXh;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY))) break;
           uint8_t* sw = smem + stage * kStageBytes2;
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (kHalfBytes + (p.tile_x >> 1) * kBK));
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (kHalfBytes + (it.xw >> 1) * kBK));
           const uint32_t fb = full_leader + stage * 8;
-          tma_load_2d_pair(sw, &mapW, fb, kb * kBK, tw * 256 + 128 * (int)rank);
-          tma_load_2d_pair(sw + kHalfBytes, &mapX, fb, kb * kBK, tx * p.tile_x + (p.tile_x >> 1) * (int)rank);
+          tma_load_2d_pair(sw, &mapW, fb, kb * kBK, it.tw * 256 + 128 * (int)rank);
+          tma_load_2d_pair(sw + kHalfBytes, mx, fb, kb * kBK, it.x0 + (it.xw >> 1) * (int)rank);
           if (++stage == kStages2) {
             stage = 0;
             phase ^= 1u;
@@ -606,8 +641,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       int it = 0;
       for (int wi = pair; wi < nwork && ok; wi += npairs, ++it) {
         const int buf = it & 1;
-        const int split = wi % p.splits;
-        const int kb0 = split * p.kb_per_split, kb1 = min(nkb, kb0 + p.kb_per_split);
+        const TcItem ti = tc_item(p, wi);
+        const uint32_t idesc = ti.xw == p.tile_x ? p.idesc : p.idesc_half;
+        const int kb0 = ti.split * p.kb_per_split, kb1 = min(nkb, kb0 + p.kb_per_split);
         if (!(ok = mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1u, ERR_WAIT_TMEM_EMPTY))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * 256);
@@ -618,7 +654,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + kHalfBytes);
 #pragma unroll
           for (int j = 0; j < kBK / 32; ++j)
-            umma2<KIND>(d_tmem, adesc + 2 * j, bdesc + 2 * j, p.idesc, (kb != kb0) || (j != 0));
+            umma2<KIND>(d_tmem, adesc + 2 * j, bdesc + 2 * j, idesc, (kb != kb0) || (j != 0));
           umma2_commit(&empty[stage], 0x3);
           if (++stage == kStages2) {
             stage = 0;
@@ -636,8 +672,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     int it = 0;
     for (int wi = pair; wi < nwork; wi += npairs, ++it) {
       const int buf = it & 1;
-      const int tile = wi / p.splits, split = wi - tile * p.splits;
-      const int tw = tile % p.tiles_w, tx = tile / p.tiles_w;
+      const TcItem ti = tc_item(p, wi);
+      const int tw = ti.tw, split = ti.split;
       if (!mbar_wait(&tfull[buf], (it >> 1) & 1, ERR_WAIT_TMEM_FULL)) break;
       tc_fence_after();
       const int n = tw * 256 + 128 * (int)rank + q * 32 + lane;
@@ -651,10 +687,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
       uint16_t* D = static_cast<uint16_t*>(p.D);
 #pragma unroll 1
-      for (int j0 = 0; j0 < p.tile_x; j0 += 32) {
+      for (int j0 = 0; j0 < ti.xw; j0 += 32) {
         uint32_t r[32];
         tmem_ld32(taddr + j0, r);
-        const int mbase = tx * p.tile_x + j0;
+        const int mbase = ti.x0 + j0;
         if (!nok || mbase >= p.M) continue;
         if (p.splits > 1) {  // raw accumulators of this K split; tc_splitk_reduce_kernel finishes
           uint32_t* dst = p.ws + ((size_t)split * p.N + n) * p.M + mbase;
@@ -738,6 +774,7 @@ __host__ __device__ constexpr uint32_t make_idesc2(int a_fmt, int n) {
 bool g_use_pair = true;
 int g_tc_splitk = -1;  // -1 automatic, else forced K splits of the CTA-pair kernel
 int g_tc_tile_x = 0;   // 0 automatic, else forced activation rows per tile (256, 192, 128)
+bool g_tc_half_tail = true;  // run the last partial round of tiles as half-width items
 bool g_tc_tile_model = false;  // the rounds model below is kept for reference, not used
 
 // Activation rows per CTA-pair tile. Tiles are dealt round-robin to the CTA
@@ -833,11 +870,14 @@ cudaError_t launch_tc2(TcParams p, const void* W, const void* X, int a_fmt, cuda
   CUtensorMap mw, mx;
   cudaError_t e;
   if ((e = make_tmap_2d_u8(&mw, W, p.K, p.N, p.K, kBK, 128, true)) != cudaSuccess) return e;
+  CUtensorMap mxh;
   p.tile_x = tc_pick_tile_x(p.M, p.N);
   if ((e = make_tmap_2d_u8(&mx, X, p.K, p.M, p.K, kBK, p.tile_x / 2, true)) != cudaSuccess) return e;
+  if ((e = make_tmap_2d_u8(&mxh, X, p.K, p.M, p.K, kBK, p.tile_x / 4, true)) != cudaSuccess) return e;
   p.tiles_w = (p.N + 255) / 256;
   p.tiles_x = (p.M + p.tile_x - 1) / p.tile_x;
   p.idesc = make_idesc2<KIND>(a_fmt, p.tile_x);
+  p.idesc_half = make_idesc2<KIND>(a_fmt, p.tile_x / 2);
   auto kern = gemm_tc2_kernel<KIND>;
   const int smem = kStages2 * kStageBytes2 + 1024 + 256;
   if ((e = ensure_smem_attr((const void*)kern, smem)) != cudaSuccess) return e;
@@ -848,7 +888,14 @@ cudaError_t launch_tc2(TcParams p, const void* W, const void* X, int a_fmt, cuda
   if (p.splits < 1) p.splits = 1;
   p.kb_per_split = (nkb + p.splits - 1) / p.splits;
   p.splits = (nkb + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
-  const int nwork = ntiles * p.splits;
+  // last partial round of full tiles -> twice as many half-width items, when
+  // they then fit in one round (4096^2: 256 = 3 x 74 + 34 tiles; 34 x 2 <= 74)
+  const int rem = ntiles % maxpairs;
+  p.n_full = ntiles;
+  if (p.splits == 1 && g_tc_half_tail && ntiles > maxpairs && rem > 0 && 2 * rem <= maxpairs &&
+      (p.tile_x / 2) % 32 == 0)
+    p.n_full = ntiles - rem;
+  const int nwork = p.splits > 1 ? ntiles * p.splits : p.n_full + 2 * (ntiles - p.n_full);
   const int pairs = nwork < maxpairs ? nwork : maxpairs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
@@ -862,7 +909,7 @@ cudaError_t launch_tc2(TcParams p, const void* W, const void* X, int a_fmt, cuda
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if ((e = cudaLaunchKernelEx(&cfg, kern, p, mw, mx)) != cudaSuccess || p.splits == 1) return e;
+  if ((e = cudaLaunchKernelEx(&cfg, kern, p, mw, mx, mxh)) != cudaSuccess || p.splits == 1) return e;
   const dim3 rgrid((p.M + 31) / 32, (p.N + 31) / 32);
   tc_splitk_reduce_kernel<KIND><<<rgrid, dim3(32, 8), 0, stream>>>(p);
   return cudaGetLastError();
@@ -903,6 +950,7 @@ unsigned int tc_device_error(bool clear) {
 
 void tc_set_splitk(int splits) { g_tc_splitk = splits; }
 void tc_set_tile_x(int rows) { g_tc_tile_x = rows; }
+void tc_set_half_tail(bool on) { g_tc_half_tail = on; }
 
 // K splits for the CTA-pair kernel: enough (tile, split) work items to give
 // most CTA pairs one, at least 4 K blocks (512 bytes of K) per split, and only

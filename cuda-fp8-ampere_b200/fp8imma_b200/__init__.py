@@ -49,6 +49,7 @@ EXT_SYMBOLS = [
     "fp8imma_set_tc_pair",
     "fp8imma_set_tc_splitk",
     "fp8imma_set_tc_tile_x",
+    "fp8imma_set_tc_half_tail",
     "fp8imma_device_error",
     "fp8imma_version",
 ]
@@ -110,6 +111,8 @@ def lib() -> ctypes.CDLL:
     L.fp8imma_set_tc_splitk.argtypes = [I]
     L.fp8imma_set_tc_tile_x.restype = I
     L.fp8imma_set_tc_tile_x.argtypes = [I]
+    L.fp8imma_set_tc_half_tail.restype = I
+    L.fp8imma_set_tc_half_tail.argtypes = [I]
     L.fp8imma_set_pdl.restype = I
     L.fp8imma_set_pdl.argtypes = [I]
     L.fp8imma_device_error.restype = ctypes.c_uint

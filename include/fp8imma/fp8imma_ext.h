@@ -149,6 +149,10 @@ int fp8imma_set_tc_splitk(int splits);
 // shape to balance the rounds of tiles over the CTA pairs; 256, 192 or 128
 // forced.
 int fp8imma_set_tc_tile_x(int rows);
+// 1 (default): when the CTA-pair kernel's last round of tiles would leave more
+// than half of the CTA pairs idle, those tiles run as two half-width items
+// each (4096 x 4096: 34 of 256 tiles); 0: all tiles at full width.
+int fp8imma_set_tc_half_tail(int enable);
 // Programmatic dependent launch (default off). When on, a GEMM may start
 // streaming its weights and reading its column scales while the previous
 // kernel in the stream is still running; activations are read, and outputs

@@ -127,3 +127,33 @@ def test_native_and_fp8wgt_tile_widths(tile_x):
     torch.cuda.synchronize()
     C = C.cpu().numpy()
     assert np.abs(C - C_o).max() <= 1e-3 * np.abs(C_o).max()
+
+
+@pytest.mark.parametrize("half_tail", [1, 0])
+@pytest.mark.parametrize("M,N,K,fmt", [(2560, 2048, 256, "e4m3"), (2304, 2560, 384, "e5m2")])
+def test_int8_half_width_tail_bitexact(cuda, half_tail, M, N, K, fmt):
+    """More tiles than CTA pairs with a short last round (80 tiles on 74
+    pairs): its tiles run as two half-width items each; bit-exact either way."""
+    L = F.lib()
+    assert L.fp8imma_set_tc_pair(1) == 0 and L.fp8imma_set_tc_half_tail(half_tail) == 0
+    try:
+        e = F.ext()
+        A, B, s, sig = inputs(M, N, K, seed=M + N, fmt=fmt)
+        b_fmt = O.FMT_E5M2 if fmt == "e5m2" else O.FMT_E4M3_REF
+        D_o, acc_o = O.gemm_ex(A, B, s, b_fmt=b_fmt, col_scale_f32=sig, global_scale=0.05, a_inv_scale=20.0,
+                               nthreads=16)
+        dA = torch.from_numpy(A.view(np.int16)).cuda().view(torch.float16)
+        D, acc = e.imma_fp8_gemm(dA, torch.from_numpy(B).cuda(), torch.from_numpy(s.view(np.int16)).cuda(),
+                                 torch.from_numpy(sig).cuda(), 0.05, 20.0, "tensor", fmt, "int8", "float16", "col",
+                                 True, None)
+        torch.cuda.synchronize()
+        assert (acc.cpu().numpy() == acc_o).all()
+        assert bits_equal(to_np_bits(D), D_o).all()
+        D_o, _, _ = O.fp8_native(A, B, sig, b_fmt=O.FMT_E5M2 if fmt == "e5m2" else O.FMT_E4M3FN)
+        D, _ = e.imma_fp8_gemm(dA, torch.from_numpy(B).cuda(), None, torch.from_numpy(sig).cuda(), 1.0, 1.0, "row",
+                               fmt, "fp8", "float16", "col", False, None)
+        torch.cuda.synchronize()
+        got, ref = D.cpu().float().numpy(), D_o.view(np.float16).astype(np.float32)
+        assert np.abs(got - ref).max() <= 2e-3 * np.abs(ref).max() + 1e-6
+    finally:
+        L.fp8imma_set_tc_half_tail(1)
