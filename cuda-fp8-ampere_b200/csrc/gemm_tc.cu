@@ -27,6 +27,9 @@
 
 using namespace fp8imma_dev;
 
+// tensor-core GEMM waits park the thread (see mbar_try_wait)
+constexpr bool kTcSuspend = true;
+
 namespace fp8imma_b200 {
 
 namespace {
@@ -181,7 +184,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
         const int tw = tile % p.tiles_w, tx = tile / p.tiles_w;
         for (int kb = 0; kb < nkb; ++kb) {
-          if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY))) break;
+          if (!(ok = mbar_wait<kTcSuspend>(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY))) break;
           uint8_t* sw = smem + stage * kStageBytes;
           mbar_arrive_expect_tx(&full[stage], kStageBytes);
           tma_load_2d(sw, &mapW, &full[stage], kb * kBK, tw * kTileW);
@@ -196,7 +199,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       for (int s = 0; s < kStages && ok; ++s) {
         // the last use of each stage is observed by the MMA issuer; waiting on
         // its release here guarantees the bytes arrived and were consumed
-        ok = mbar_wait(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY);
+        ok = mbar_wait<kTcSuspend>(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY);
         if (++stage == kStages) {
           stage = 0;
           phase ^= 1u;
@@ -212,11 +215,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       int it = 0;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
         const int buf = it & 1;
-        if (!(ok = mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1u, ERR_WAIT_TMEM_EMPTY))) break;
+        if (!(ok = mbar_wait<kTcSuspend>(&tempty[buf], ((it >> 1) & 1) ^ 1u, ERR_WAIT_TMEM_EMPTY))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * kTileX);
         for (int kb = 0; kb < nkb; ++kb) {
-          if (!(ok = mbar_wait(&full[stage], phase, ERR_WAIT_FULL))) break;
+          if (!(ok = mbar_wait<kTcSuspend>(&full[stage], phase, ERR_WAIT_FULL))) break;
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * kStageBytes);
           const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + kBytesW);
@@ -232,7 +235,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         umma_commit(&tfull[buf]);
       }
       umma_commit(drain);
-      mbar_wait(drain, 0, ERR_WAIT_FULL);
+      mbar_wait<kTcSuspend>(drain, 0, ERR_WAIT_FULL);
     }
   } else {
     // ------------------------------------------------------ epilogue
@@ -241,7 +244,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
       const int buf = it & 1;
       const int tw = tile % p.tiles_w, tx = tile / p.tiles_w;
-      if (!mbar_wait(&tfull[buf], (it >> 1) & 1, ERR_WAIT_TMEM_FULL)) break;
+      if (!mbar_wait<kTcSuspend>(&tfull[buf], (it >> 1) & 1, ERR_WAIT_TMEM_FULL)) break;
       tc_fence_after();
       const int n = tw * kTileW + q * 32 + lane;
       const bool nok = n < p.N;
@@ -612,7 +615,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         const int kb0 = it.split * p.kb_per_split, kb1 = min(nkb, kb0 + p.kb_per_split);
         const CUtensorMap* mx = it.xw == p.tile_x ? &mapX : &mapXh;
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY))) break;
+          if (!(ok = mbar_wait<kTcSuspend>(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY))) break;
           uint8_t* sw = smem + stage * kStageBytes2;
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (kHalfBytes + (it.xw >> 1) * kBK));
           const uint32_t fb = full_leader + stage * 8;
@@ -625,7 +628,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         }
       }
       for (int s = 0; s < kStages2 && ok; ++s) {  // drain: all issued loads consumed
-        ok = mbar_wait(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY);
+        ok = mbar_wait<kTcSuspend>(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY);
         if (++stage == kStages2) {
           stage = 0;
           phase ^= 1u;
@@ -644,11 +647,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         const TcItem ti = tc_item(p, wi);
         const uint32_t idesc = ti.xw == p.tile_x ? p.idesc : p.idesc_half;
         const int kb0 = ti.split * p.kb_per_split, kb1 = min(nkb, kb0 + p.kb_per_split);
-        if (!(ok = mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1u, ERR_WAIT_TMEM_EMPTY))) break;
+        if (!(ok = mbar_wait<kTcSuspend>(&tempty[buf], ((it >> 1) & 1) ^ 1u, ERR_WAIT_TMEM_EMPTY))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * 256);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!(ok = mbar_wait(&full[stage], phase, ERR_WAIT_FULL))) break;
+          if (!(ok = mbar_wait<kTcSuspend>(&full[stage], phase, ERR_WAIT_FULL))) break;
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * kStageBytes2);
           const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + kHalfBytes);
@@ -664,7 +667,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         umma2_commit(&tfull[buf], 0x3);
       }
       umma2_commit(drain, 0x1);
-      mbar_wait(drain, 0, ERR_WAIT_FULL);
+      mbar_wait<kTcSuspend>(drain, 0, ERR_WAIT_FULL);
     }
   } else {
     // ---- epilogue (both CTAs): this CTA's 128 TMEM lanes = 128 weight columns
@@ -674,7 +677,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const int buf = it & 1;
       const TcItem ti = tc_item(p, wi);
       const int tw = ti.tw, split = ti.split;
-      if (!mbar_wait(&tfull[buf], (it >> 1) & 1, ERR_WAIT_TMEM_FULL)) break;
+      if (!mbar_wait<kTcSuspend>(&tfull[buf], (it >> 1) & 1, ERR_WAIT_TMEM_FULL)) break;
       tc_fence_after();
       const int n = tw * 256 + 128 * (int)rank + q * 32 + lane;
       const bool nok = n < p.N;

@@ -59,25 +59,41 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// kSuspend: let the hardware park the waiting thread until the phase
+// completes (or a time hint passes) instead of returning at once; the
+// tensor-core GEMMs, whose epilogue and producer warps wait through whole
+// tiles, use it so that those waits do not spin.
+template <bool kSuspend = false>
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
+  if (kSuspend) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000000;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+  }
   return ok != 0;
 }
 
 // Bounded wait for the phase with the given parity to complete: gives up
 // after kWaitLimitNs of wall time, records err_code and returns false.
+template <bool kSuspend = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int err_code) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait<kSuspend>(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (unsigned int i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait<kSuspend>(bar, parity)) return true;
     if (globaltimer_ns() - t0 > kWaitLimitNs) break;
   }
   atomicCAS(&g_fp8imma_device_error, 0u, err_code);
