@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         }
         const int mcount = min(32, p.M - mbase);
         if (p.out_row_major) {
-          for (int j = 0; j < mcount; ++j) D[(size_t)(mbase + j) * p.N + n] = o[j];
+          _Pragma("unroll") for (int j = 0; j < 32; ++j) if (j < mcount) D[(size_t)(mbase + j) * p.N + n] = o[j];
         } else {
           uint16_t* dst = D + (size_t)n * p.M + mbase;
           if (mcount == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
@@ -295,11 +295,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
               reinterpret_cast<uint4*>(dst)[v4] = w;
             }
           } else {
-            for (int j = 0; j < mcount; ++j) dst[j] = o[j];
+            _Pragma("unroll") for (int j = 0; j < 32; ++j) if (j < mcount) dst[j] = o[j];
           }
         }
         if (KIND == KIND_I8 && p.acc_out) {
-          for (int j = 0; j < mcount; ++j) p.acc_out[(size_t)n * p.M + mbase + j] = (int32_t)r[j];
+          _Pragma("unroll") for (int j = 0; j < 32; ++j) if (j < mcount) p.acc_out[(size_t)n * p.M + mbase + j] = (int32_t)r[j];
         }
       }
       tc_fence_before();
@@ -703,14 +703,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             for (int v4 = 0; v4 < 8; ++v4)
               reinterpret_cast<uint4*>(dst)[v4] = make_uint4(r[4 * v4], r[4 * v4 + 1], r[4 * v4 + 2], r[4 * v4 + 3]);
           } else {
-            for (int j = 0; j < mc; ++j) dst[j] = r[j];
+            _Pragma("unroll") for (int j = 0; j < 32; ++j) if (j < mc) dst[j] = r[j];
           }
           continue;
         }
         if (KIND == KIND_F16) {  // fp8wgt: fp32 accumulators straight to row-major C[m, n]
           float* C = static_cast<float*>(p.D);
           const int mc = min(32, p.M - mbase);
-          for (int j = 0; j < mc; ++j) C[(size_t)(mbase + j) * p.N + n] = __uint_as_float(r[j]);
+          _Pragma("unroll") for (int j = 0; j < 32; ++j) if (j < mc) C[(size_t)(mbase + j) * p.N + n] = __uint_as_float(r[j]);
           continue;
         }
         uint16_t o[32];
@@ -730,7 +730,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         }
         const int mcount = min(32, p.M - mbase);
         if (p.out_row_major) {
-          for (int j = 0; j < mcount; ++j) D[(size_t)(mbase + j) * p.N + n] = o[j];
+          _Pragma("unroll") for (int j = 0; j < 32; ++j) if (j < mcount) D[(size_t)(mbase + j) * p.N + n] = o[j];
         } else {
           uint16_t* dst = D + (size_t)n * p.M + mbase;
           if (mcount == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
@@ -744,11 +744,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
               reinterpret_cast<uint4*>(dst)[v4] = w;
             }
           } else {
-            for (int j = 0; j < mcount; ++j) dst[j] = o[j];
+            _Pragma("unroll") for (int j = 0; j < 32; ++j) if (j < mcount) dst[j] = o[j];
           }
         }
         if (KIND == KIND_I8 && p.acc_out) {
-          for (int j = 0; j < mcount; ++j) p.acc_out[(size_t)n * p.M + mbase + j] = (int32_t)r[j];
+          _Pragma("unroll") for (int j = 0; j < 32; ++j) if (j < mcount) p.acc_out[(size_t)n * p.M + mbase + j] = (int32_t)r[j];
         }
       }
       tc_fence_before();
