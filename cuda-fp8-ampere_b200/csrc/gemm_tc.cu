@@ -405,7 +405,10 @@ __global__ void __launch_bounds__(256) transcode_b_kernel(const uint8_t* __restr
 // Native path: per-row E4M3 quantisation. One CTA (256 threads) per row:
 // absmax over to_half(a), row scale s = absmax/448, a8 = e4m3_rn_satfinite(a *
 // (448/absmax)). K % 8 == 0.
-template <int AT>
+// VPT > 0: the row is held in registers (VPT 16-byte vectors per thread,
+// K <= VPT * 2048) between the absmax and the conversion, so it is read once;
+// VPT == 0 reads it twice (any K).
+template <int AT, int VPT>
 __global__ void __launch_bounds__(256) quant_a_e4m3_kernel(const void* __restrict__ A, int M, int K,
                                                            uint8_t* __restrict__ Aq, float* __restrict__ row_scale) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // see quant_a_s8_kernel
@@ -413,16 +416,28 @@ __global__ void __launch_bounds__(256) quant_a_e4m3_kernel(const void* __restric
   if (m >= M) return;
   const uint16_t* row = static_cast<const uint16_t*>(A) + (size_t)m * K;
   __shared__ float red[8];
+  constexpr int kRegs = VPT > 0 ? VPT : 1;
+  uint4 keep[kRegs];
   float amax = 0.0f;
-  for (int k = threadIdx.x * 8; k < K; k += 256 * 8) {
-    uint4 v = *reinterpret_cast<const uint4*>(row + k);
-    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  auto absmax8 = [&](const uint4& v) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       uint32_t h2 = AT == A_BF16 ? bf16x2_to_f16x2(w[j]) : w[j];
       float2 f = __half22float2(*reinterpret_cast<__half2*>(&h2));
       amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
     }
+  };
+  if (VPT > 0) {
+#pragma unroll
+    for (int i = 0; i < kRegs; ++i) {
+      const int k = (threadIdx.x + 256 * i) * 8;
+      keep[i] = k < K ? *reinterpret_cast<const uint4*>(row + k) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < kRegs; ++i) absmax8(keep[i]);
+  } else {
+    for (int k = threadIdx.x * 8; k < K; k += 256 * 8) absmax8(*reinterpret_cast<const uint4*>(row + k));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -438,9 +453,8 @@ __global__ void __launch_bounds__(256) quant_a_e4m3_kernel(const void* __restric
   }
   if (threadIdx.x == 0) row_scale[m] = s;
   uint8_t* out = Aq + (size_t)m * K;
-  for (int k = threadIdx.x * 8; k < K; k += 256 * 8) {
-    uint4 v = *reinterpret_cast<const uint4*>(row + k);
-    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  auto convert8 = [&](const uint4& v, int k) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
     uint32_t o[2];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
@@ -454,9 +468,27 @@ __global__ void __launch_bounds__(256) quant_a_e4m3_kernel(const void* __restric
       o[j] = (uint32_t)lo | ((uint32_t)hi << 16);
     }
     *reinterpret_cast<uint2*>(out + k) = make_uint2(o[0], o[1]);
+  };
+  if (VPT > 0) {
+#pragma unroll
+    for (int i = 0; i < kRegs; ++i) {
+      const int k = (threadIdx.x + 256 * i) * 8;
+      if (k < K) convert8(keep[i], k);
+    }
+  } else {
+    for (int k = threadIdx.x * 8; k < K; k += 256 * 8) convert8(*reinterpret_cast<const uint4*>(row + k), k);
   }
 }
 
+template <int AT>
+void launch_quant_e4m3_rows(const void* A, int M, int K, uint8_t* Aq, float* rs, cudaStream_t stream) {
+  const int vpt = (K + 2047) / 2048;
+  if (vpt <= 1) quant_a_e4m3_kernel<AT, 1><<<M, 256, 0, stream>>>(A, M, K, Aq, rs);
+  else if (vpt <= 2) quant_a_e4m3_kernel<AT, 2><<<M, 256, 0, stream>>>(A, M, K, Aq, rs);
+  else if (vpt <= 4) quant_a_e4m3_kernel<AT, 4><<<M, 256, 0, stream>>>(A, M, K, Aq, rs);
+  else if (vpt <= 8) quant_a_e4m3_kernel<AT, 8><<<M, 256, 0, stream>>>(A, M, K, Aq, rs);
+  else quant_a_e4m3_kernel<AT, 0><<<M, 256, 0, stream>>>(A, M, K, Aq, rs);
+}
 
 // ---------------------------------------------------------------- 2-SM ----
 // cta_group::2 variant: a cluster of two CTAs computes a 256 (weight columns)
@@ -1058,8 +1090,8 @@ cudaError_t launch_quant_a_s8(const void* A, int a_type, int M, int K, uint16_t 
 // Per-row E4M3 activation quantisation alone (small-M native path).
 cudaError_t launch_quant_a_e4m3(const void* A, int a_type, int M, int K, uint8_t* Aq, float* row_scale,
                                 cudaStream_t stream) {
-  if (a_type == A_BF16) quant_a_e4m3_kernel<A_BF16><<<M, 256, 0, stream>>>(A, M, K, Aq, row_scale);
-  else quant_a_e4m3_kernel<A_F16><<<M, 256, 0, stream>>>(A, M, K, Aq, row_scale);
+  if (a_type == A_BF16) launch_quant_e4m3_rows<A_BF16>(A, M, K, Aq, row_scale, stream);
+  else launch_quant_e4m3_rows<A_F16>(A, M, K, Aq, row_scale, stream);
   return cudaGetLastError();
 }
 
@@ -1070,8 +1102,8 @@ cudaError_t launch_gemm_tc_fp8(const void* A, int a_type, const uint8_t* B, int 
                                cudaStream_t stream) {
   uint8_t* Aq = static_cast<uint8_t*>(scratch);
   float* rs = reinterpret_cast<float*>(Aq + (((size_t)M * K + 255) & ~size_t(255)));
-  if (a_type == A_BF16) quant_a_e4m3_kernel<A_BF16><<<M, 256, 0, stream>>>(A, M, K, Aq, rs);
-  else quant_a_e4m3_kernel<A_F16><<<M, 256, 0, stream>>>(A, M, K, Aq, rs);
+  if (a_type == A_BF16) launch_quant_e4m3_rows<A_BF16>(A, M, K, Aq, rs, stream);
+  else launch_quant_e4m3_rows<A_F16>(A, M, K, Aq, rs, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   CUtensorMap mw, mx;

@@ -28,7 +28,10 @@ struct Ptrs8 {
   unsigned long long p[8];
 };
 
-__global__ void __launch_bounds__(kGatherThreads) peer_gather_kernel(Ptrs8 outs, Ptrs8 pads, int world, int rank,
+// (__grid_constant__: the pointer tables are indexed at run time and read in
+// place from parameter space instead of being copied to a local stack)
+__global__ void __launch_bounds__(kGatherThreads) peer_gather_kernel(const __grid_constant__ Ptrs8 outs,
+                                                                     const __grid_constant__ Ptrs8 pads, int world, int rank,
                                                                      unsigned long long byte0, unsigned long long nbytes,
                                                                      unsigned int epoch_arg) {
   // 1. copy this rank's rows to every peer (grid-strided). byte0 = rank * N *
