@@ -353,14 +353,13 @@ __device__ __forceinline__ void store_out(const GemvParams& p, int n, int m, int
 // Column-parallel output gather fused into the epilogue (world > 1): the
 // CTA's finished outputs (columns [n_lo, n_hi), rows [m0, m0+MR) of this
 // rank's slice, already stored locally) are copied into the same place of
-// every peer's full output with 16-byte stores over NVLink, then published
-// with one system-scope release increment of this rank's counter in each
-// peer's signal pad (slots kPeerFusedSlot + rank). The first CTA of the grid
-// then advances this rank's call epoch (slot kPeerFusedEpochSlot of its own
-// pad) and waits (bounded) until every peer's counter in its own pad has
-// reached epoch x (CTAs per grid): all peers' slices have landed.
-__device__ __forceinline__ void peer_publish(const GemvParams& p, int n_lo, int n_hi, int m0, int MR,
-                                             unsigned int* target_s) {
+// every peer's full output with 16-byte stores over NVLink. Publication
+// (peer_signal_and_wait): one system-scope release increment per cluster of
+// this rank's counter in each peer's signal pad (slots kPeerFusedSlot +
+// rank); the first CTA of the grid then advances this rank's call epoch (slot
+// kPeerFusedEpochSlot of its own pad) and waits (bounded) until every peer's
+// counter in its own pad has reached epoch x (clusters per grid).
+__device__ __forceinline__ void peer_copy(const GemvParams& p, int n_lo, int n_hi, int m0, int MR) {
   __syncthreads();  // this CTA's local output stores are done
   const int m1 = min(p.M, m0 + MR);
   if (n_lo < n_hi && m0 < m1) {
@@ -391,7 +390,15 @@ __device__ __forceinline__ void peer_publish(const GemvParams& p, int n_lo, int 
       }
     }
   }
-  __syncthreads();  // every copy of this CTA is issued before the release below
+}
+
+// After the cluster barrier that ends the kernel (which orders every CTA's
+// peer stores of the cluster before it): the cluster's first CTA publishes
+// them with one system-scope release per peer, and the grid's first CTA waits
+// until every peer has published all of its clusters for this call.
+__device__ __forceinline__ void peer_signal_and_wait(const GemvParams& p, unsigned int cluster_rank,
+                                                     unsigned int clusters, unsigned int* target_s) {
+  if (cluster_rank != 0) return;
   if ((int)threadIdx.x < p.world && (int)threadIdx.x != p.rank) {
     unsigned int* slot = reinterpret_cast<unsigned int*>(p.peer_sig[threadIdx.x]) + kPeerFusedSlot + p.rank;
     asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(slot) : "memory");
@@ -404,7 +411,7 @@ __device__ __forceinline__ void peer_publish(const GemvParams& p, int n_lo, int 
       e = *ctr + 1;
       *ctr = e;
     }
-    *target_s = e * (gridDim.x * gridDim.y * gridDim.z);
+    *target_s = e * clusters;
   }
   __syncthreads();
   const unsigned int target = *target_s;
@@ -600,11 +607,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
   if (threadIdx.x == 0) TRACE_POINT(p, 7);
-  if (p.world > 1)
-    peer_publish(p, tile_n0 + rank * cols_per, min(p.N, tile_n0 + (rank + 1) * cols_per), m0, MR,
-                 reinterpret_cast<unsigned int*>(smem + kBarOffset + 128));
+  if (p.world > 1) peer_copy(p, tile_n0 + rank * cols_per, min(p.N, tile_n0 + (rank + 1) * cols_per), m0, MR);
   cluster.sync();  // keep shared memory alive until every peer has read it
   if (threadIdx.x == 0) TRACE_POINT(p, 8);
+  if (p.world > 1)
+    peer_signal_and_wait(p, (unsigned int)rank, (gridDim.x * gridDim.y * gridDim.z) / (unsigned int)S,
+                         reinterpret_cast<unsigned int*>(smem + kBarOffset + 128));
 }
 
 // ---------------------------------------------------------------------------
