@@ -570,6 +570,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   const float* cs_s = reinterpret_cast<const float*>(smem + kColScaleOffset);
   const float* rg_s = reinterpret_cast<const float*>(smem + kRowScaleOffset);
   constexpr int kEpiBatch = 4;  // partial-sum reads in flight per thread
+  const int32_t* peer_part[8];  // distributed shared memory address of each cluster rank's partials
+#pragma unroll
+  for (int q = 0; q < 8; ++q) peer_part[q] = q < S ? cluster.map_shared_rank(part, q) : part;
   for (int base = threadIdx.x; base < nelem; base += kEpiBatch * kThreads) {
     int32_t sum[kEpiBatch];
     int lcs[kEpiBatch], mrs[kEpiBatch];
@@ -589,10 +592,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       int32_t acc_s = 0;
       float acc_f = 0.0f;
       if (e < nelem) {
-        for (int q = 0; q < S; ++q) {
-          const int32_t v = cluster.map_shared_rank(part, q)[lc * MR + mr];
-          if (is_float_acc<FMT>()) acc_f += __int_as_float(v);
-          else acc_s += v;
+        // all S remote partials of the element in flight at once, summed in rank order
+        int32_t v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[q] = q < S ? peer_part[q][lc * MR + mr] : 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (q >= S) break;
+          if (is_float_acc<FMT>()) acc_f += __int_as_float(v[q]);
+          else acc_s += v[q];
         }
       }
       sum[j] = is_float_acc<FMT>() ? __float_as_int(acc_f) : acc_s;
