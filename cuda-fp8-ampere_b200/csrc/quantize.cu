@@ -1,0 +1,109 @@
+// FP16 / BF16 / FP32 weights -> FP8 bytes with a per-column scale: the
+// weight format the GEMM path consumes (one row of B per output column).
+//
+//   sigma_n = max(absmax_k |w[n,k]|, 1e-30) / fmax          (fp32, IEEE divide)
+//   B[n,k]  = fp8_rne_satfinite(w[n,k] / sigma_n)           (fp32, IEEE divide)
+//   step_n  = fp16_rn(max_k |decode(B[n,k])| / 127)         (reference-API int8 step)
+//
+// Formats: E4M3FN (fmax 448), E5M2 (fmax 57344), and E4M3 within the range of
+// the reference decode table (fmax 240: no exponent-15 codes, which that table
+// reads as Inf / NaN). The reference ships only an approximate per-tensor
+// device encoder for its benchmarks (src/bench/bench_fp8_quant_cublas.inl:2-38,
+// clamping at 240); this is the exact per-column form the benchmark
+// definition describes. Weights must be finite.
+#include "fp8imma/fp8imma_ext.h"
+#include "fp8imma_kernels.h"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace fp8imma_b200 {
+namespace {
+
+constexpr int kQThreads = 256;
+
+template <int WT>
+__device__ __forceinline__ float load_w(const void* W, size_t i) {
+  if (WT == FP8IMMA_W_F32) return static_cast<const float*>(W)[i];
+  if (WT == FP8IMMA_W_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(W)[i]);
+  return __half2float(static_cast<const __half*>(W)[i]);
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();  // red may still be read from a previous reduction
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  v = red[0];
+#pragma unroll
+  for (int i = 1; i < kQThreads / 32; ++i) v = fmaxf(v, red[i]);
+  return v;
+}
+
+// one CTA per weight row (output column)
+template <int WT, int FMT>
+__global__ void __launch_bounds__(kQThreads) quantize_rows_kernel(const void* __restrict__ W, int N, int K,
+                                                                  uint8_t* __restrict__ B, float* __restrict__ sigma,
+                                                                  uint16_t* __restrict__ step) {
+  __shared__ float red[kQThreads / 32];
+  const int n = blockIdx.x;
+  if (n >= N) return;
+  const size_t base = (size_t)n * K;
+  float amax = 0.0f;
+  for (int k = threadIdx.x; k < K; k += kQThreads) amax = fmaxf(amax, fabsf(load_w<WT>(W, base + k)));
+  amax = block_max(amax, red);
+  const float fmax_v = FMT == FP8IMMA_Q_E5M2 ? 57344.0f : (FMT == FP8IMMA_Q_E4M3_REF ? 240.0f : 448.0f);
+  const float s = __fdiv_rn(fmaxf(amax, 1e-30f), fmax_v);
+  float dmax = 0.0f;
+  for (int k = threadIdx.x; k < K; k += kQThreads) {
+    float x = __fdiv_rn(load_w<WT>(W, base + k), s);
+    if (FMT == FP8IMMA_Q_E4M3_REF) x = fminf(fmaxf(x, -240.0f), 240.0f);
+    uint16_t two;
+    uint32_t h2;
+    if (FMT == FP8IMMA_Q_E5M2) {
+      asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(two) : "f"(0.0f), "f"(x));
+      asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(h2) : "h"(two));
+    } else {
+      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(two) : "f"(0.0f), "f"(x));
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(two));
+    }
+    B[base + k] = (uint8_t)(two & 0xFFu);
+    dmax = fmaxf(dmax, fabsf(__half2float(__ushort_as_half((uint16_t)(h2 & 0xFFFFu)))));
+  }
+  dmax = block_max(dmax, red);
+  if (threadIdx.x == 0) {
+    if (sigma) sigma[n] = s;
+    if (step) step[n] = __half_as_ushort(__float2half_rn(__fdiv_rn(dmax, 127.0f)));
+  }
+}
+
+template <int WT>
+cudaError_t launch_q(const void* W, int N, int K, int fmt, uint8_t* B, float* sigma, uint16_t* step,
+                     cudaStream_t st) {
+  switch (fmt) {
+    case FP8IMMA_Q_E4M3FN: quantize_rows_kernel<WT, FP8IMMA_Q_E4M3FN><<<N, kQThreads, 0, st>>>(W, N, K, B, sigma, step); break;
+    case FP8IMMA_Q_E5M2: quantize_rows_kernel<WT, FP8IMMA_Q_E5M2><<<N, kQThreads, 0, st>>>(W, N, K, B, sigma, step); break;
+    case FP8IMMA_Q_E4M3_REF: quantize_rows_kernel<WT, FP8IMMA_Q_E4M3_REF><<<N, kQThreads, 0, st>>>(W, N, K, B, sigma, step); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace fp8imma_b200
+
+using namespace fp8imma_b200;
+
+extern "C" int fp8imma_quantize_weights(const void* W, int w_type, int N, int K, int fmt, void* B_out,
+                                        float* col_scale_out, uint16_t* step_out, void* stream) {
+  if (N <= 0 || K <= 0) return (int)cudaErrorInvalidConfiguration;
+  if (!W || !B_out || w_type < 0 || w_type > 2 || fmt < 0 || fmt > 2) return (int)cudaErrorInvalidValue;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* B = static_cast<uint8_t*>(B_out);
+  switch (w_type) {
+    case FP8IMMA_W_F16: return (int)launch_q<FP8IMMA_W_F16>(W, N, K, fmt, B, col_scale_out, step_out, st);
+    case FP8IMMA_W_BF16: return (int)launch_q<FP8IMMA_W_BF16>(W, N, K, fmt, B, col_scale_out, step_out, st);
+    default: return (int)launch_q<FP8IMMA_W_F32>(W, N, K, fmt, B, col_scale_out, step_out, st);
+  }
+}

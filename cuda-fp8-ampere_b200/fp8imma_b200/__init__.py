@@ -41,6 +41,7 @@ EXT_SYMBOLS = [
     "fp8imma_gemm_allgather",
     "fp8imma_set_fused_gather",
     "fp8imma_fp8wgt_linear_forward",
+    "fp8imma_quantize_weights",
     "fp8imma_set_splitk",
     "fp8imma_set_stream_k",
     "fp8imma_set_small_m_max",
@@ -97,6 +98,8 @@ def lib() -> ctypes.CDLL:
     L.fp8imma_gemm_allgather.argtypes = [ctypes.POINTER(FP8ImmaGemmArgs), P, P, I, I, ctypes.c_uint, P]
     L.fp8imma_gemm_rowquant_noalloc.restype = I
     L.fp8imma_gemm_rowquant_noalloc.argtypes = [ctypes.POINTER(FP8ImmaGemmArgs), P]
+    L.fp8imma_quantize_weights.restype = I
+    L.fp8imma_quantize_weights.argtypes = [P, I, I, I, I, P, P, P, P]
     L.fp8imma_fp8wgt_linear_forward.restype = I
     L.fp8imma_fp8wgt_linear_forward.argtypes = [P, P, F, P, I, I, I, P]
     L.fp8imma_set_splitk.restype = I

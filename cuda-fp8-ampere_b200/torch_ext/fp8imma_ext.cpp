@@ -156,6 +156,32 @@ std::vector<torch::Tensor> imma_fp8_gemm(torch::Tensor A, torch::Tensor B, c10::
   return {D, acc.defined() ? acc : torch::Tensor()};
 }
 
+// Weight quantiser (fp8imma_quantize_weights): W [N,K] fp16/bf16/fp32 CUDA
+// tensor -> (B [N,K] uint8, sigma [N] fp32, step [N] int16 fp16 bits).
+std::vector<torch::Tensor> quantize_weights(torch::Tensor W, std::string fmt) {
+  TORCH_CHECK(W.is_cuda() && W.is_contiguous() && W.dim() == 2, "W must be a contiguous 2-D CUDA tensor");
+  int wt;
+  if (W.scalar_type() == at::kHalf) wt = FP8IMMA_W_F16;
+  else if (W.scalar_type() == at::kBFloat16) wt = FP8IMMA_W_BF16;
+  else if (W.scalar_type() == at::kFloat) wt = FP8IMMA_W_F32;
+  else TORCH_CHECK(false, "W must be fp16, bf16 or fp32");
+  int f;
+  if (fmt == "e4m3") f = FP8IMMA_Q_E4M3FN;
+  else if (fmt == "e5m2") f = FP8IMMA_Q_E5M2;
+  else if (fmt == "e4m3_ref") f = FP8IMMA_Q_E4M3_REF;
+  else TORCH_CHECK(false, "fmt must be 'e4m3', 'e5m2' or 'e4m3_ref'");
+  const int64_t N = W.size(0), K = W.size(1);
+  const c10::cuda::CUDAGuard guard(W.device());
+  auto B = torch::empty({N, K}, W.options().dtype(torch::kUInt8));
+  auto sigma = torch::empty({N}, W.options().dtype(torch::kFloat));
+  auto step = torch::empty({N}, W.options().dtype(torch::kShort));
+  check_launch(fp8imma_quantize_weights(W.data_ptr(), wt, (int)N, (int)K, f, B.data_ptr(), sigma.data_ptr<float>(),
+                                        reinterpret_cast<uint16_t*>(step.data_ptr<int16_t>()),
+                                        (void*)at::cuda::getCurrentCUDAStream()),
+               "fp8imma_quantize_weights");
+  return {B, sigma, step};
+}
+
 int64_t last_path() { return fp8imma_last_path(); }
 int64_t set_splitk(int64_t s) { return fp8imma_set_splitk((int)s); }
 int64_t set_small_m_max(int64_t m) { return fp8imma_set_small_m_max((int)m); }
@@ -173,6 +199,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("path") = "int8", py::arg("out_dtype") = "float16", py::arg("out_layout") = "col",
         py::arg("return_acc") = false, py::arg("out") = py::none(), py::arg("a_host") = py::none(),
         py::arg("out_host") = py::none());
+  m.def("quantize_weights", &quantize_weights, "FP8 weight quantiser with per-column scales (see fp8imma_ext.h)",
+        py::arg("W"), py::arg("fmt") = "e4m3");
   m.def("last_path", &last_path, "kernel family of the last call on this thread");
   m.def("set_splitk", &set_splitk, "force the small-M K split (0 = automatic)");
   m.def("set_small_m_max", &set_small_m_max, "largest M for the small-M kernel");

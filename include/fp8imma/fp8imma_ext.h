@@ -69,6 +69,22 @@ int fp8imma_gemm(const fp8imma_gemm_args* args, void* stream);
 // args->D are the caller's device staging buffers.
 int fp8imma_gemm_host_io(const fp8imma_gemm_args* args, const void* A_host, void* D_host, void* stream);
 
+// Weight quantiser (no reference counterpart beyond an approximate per-tensor
+// benchmark encoder): W [N,K] (fp16 / bf16 / fp32, finite) -> FP8 bytes
+// B_out [N,K] with a per-row (= per output column) scale:
+//   sigma_n = max(absmax_k |W[n,k]|, 1e-30) / fmax, B = fp8_rne_satfinite(W / sigma_n),
+// col_scale_out[n] = sigma_n (fp32, the native path's column scale; may be
+// null), step_out[n] = fp16(max_k |decode(B[n,k])| / 127) (the int8 step the
+// reference API takes as col_scales; may be null).
+enum fp8imma_w_type { FP8IMMA_W_F16 = 0, FP8IMMA_W_BF16 = 1, FP8IMMA_W_F32 = 2 };
+enum fp8imma_q_format {
+  FP8IMMA_Q_E4M3FN = 0,   // fmax 448 (hardware E4M3FN range)
+  FP8IMMA_Q_E5M2 = 1,     // fmax 57344
+  FP8IMMA_Q_E4M3_REF = 2  // fmax 240: codes the reference decode table reads as finite
+};
+int fp8imma_quantize_weights(const void* W, int w_type, int N, int K, int fmt, void* B_out, float* col_scale_out,
+                             uint16_t* step_out, void* stream);
+
 // Largest M accepted by fp8imma_gemm_rowquant_noalloc.
 #define FP8IMMA_NOALLOC_MAX_M 4096
 

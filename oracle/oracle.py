@@ -245,3 +245,46 @@ def _encode_fp8(x: np.ndarray, mbits: int, bias: int, maxv: float) -> np.ndarray
     code = np.where(v == 0, 0, code).astype(np.uint8)
     out = sign | code
     return np.where(nan, np.uint8(0x7F), out).astype(np.uint8)
+
+
+def e4m3fn_decode(b: np.ndarray) -> np.ndarray:
+    """E4M3FN bytes -> float32 (OCP semantics: exponent 15 finite except 0x7F/0xFF NaN)."""
+    b = np.asarray(b, np.uint8).astype(np.int64)
+    s = np.where(b & 0x80, -1.0, 1.0)
+    e = (b >> 3) & 0xF
+    m = b & 7
+    v = np.where(e == 0, m * 2.0 ** -9, (1.0 + m / 8.0) * np.ldexp(1.0, e - 7))
+    v = np.where((b & 0x7F) == 0x7F, np.nan, v)
+    return (s * v).astype(np.float32)
+
+
+def e5m2_decode(b: np.ndarray) -> np.ndarray:
+    """E5M2 bytes -> float32 (fp16 bits b << 8)."""
+    return (np.asarray(b, np.uint8).astype(np.uint16) << 8).view(np.float16).astype(np.float32)
+
+
+def quantize_weights(W: np.ndarray, fmt: str = "e4m3"):
+    """Per-column FP8 weight quantiser, restated from the GEMM path's weight
+    recipe (finite weights): sigma_n = float32(max(absmax_n, 1e-30) / fmax),
+    B = fp8_rne_satfinite(float32(W / sigma_n)) (E4M3FN 448, E5M2 57344, or
+    E4M3 clamped at 240, the largest value the reference decode table reads
+    as finite; the reference's own benchmark encoder clamps there too,
+    src/bench/bench_fp8_quant_cublas.inl:2-38, but is per tensor and
+    approximate), step_n = fp16(float32(max |decode(B_n)|) / 127).
+    Returns (B uint8 [N,K], sigma float32 [N], step uint16 fp16 bits [N])."""
+    W = np.asarray(W, np.float32)
+    fmax = {"e4m3": 448.0, "e5m2": 57344.0, "e4m3_ref": 240.0}[fmt]
+    amax = np.maximum(np.abs(W).max(axis=1), np.float32(1e-30)).astype(np.float32)
+    sigma = (amax / np.float32(fmax)).astype(np.float32)
+    x = (W / sigma[:, None]).astype(np.float32)
+    if fmt == "e4m3_ref":
+        x = np.clip(x, np.float32(-240.0), np.float32(240.0))
+    if fmt == "e5m2":
+        B = e5m2_encode(x)
+        dec = e5m2_decode(B)
+    else:
+        B = e4m3fn_encode(x)
+        dec = e4m3fn_decode(B)
+    dmax = np.abs(dec).max(axis=1).astype(np.float32)
+    step = (dmax / np.float32(127.0)).astype(np.float16).view(np.uint16)
+    return B, sigma, step
