@@ -120,6 +120,10 @@ static int ref_launch(int kChunk, int a_type, int group, const void* A, const vo
 
 // Native FP8 path: activations quantised per row to E4M3, weights used as raw
 // E4M3FN / E5M2 bytes, fp32 accumulation, D = acc * row_scale * col_scale.
+// Fused epilogue of the current fp8imma_gemm_epilogue call on this thread.
+thread_local const float* t_bias = nullptr;
+thread_local int t_act = 0;
+
 static cudaError_t gemm_native(const fp8imma_gemm_args* a, cudaStream_t stream) {
   if (a->M <= 0 || a->N <= 0) return cudaErrorInvalidConfiguration;
   if (a->K <= 0 || !a->A || !a->B || !a->D || !a->col_scales_f32) return cudaErrorInvalidValue;
@@ -149,6 +153,8 @@ static cudaError_t gemm_native(const fp8imma_gemm_args* a, cudaStream_t stream) 
       p.keff_a = a->K;
       p.out_bf16 = a->out_type;
       p.out_row_major = a->out_layout;
+      p.bias = t_bias;
+      p.act = t_act;
       t_last_path = 5;
       p.pdl = 1;  // weights stream while the quantisation kernel finishes; rows and scales are read after it
       e = launch_gemv_s8(p, A_S8, a->b_format == FP8IMMA_B_E5M2 ? 3 : 2, g_splitk.load(), stream);
@@ -156,7 +162,7 @@ static cudaError_t gemm_native(const fp8imma_gemm_args* a, cudaStream_t stream) 
   } else {
     t_last_path = 4;
     e = launch_gemm_tc_fp8(a->A, a->a_type, static_cast<const uint8_t*>(a->B), a->b_format, a->col_scales_f32,
-                           a->D, a->M, a->N, a->K, a->out_type, a->out_layout, scratch, stream);
+                           a->D, a->M, a->N, a->K, a->out_type, a->out_layout, scratch, stream, t_bias, t_act);
   }
   cudaError_t e2 = cudaFreeAsync(scratch, stream);
   return e != cudaSuccess ? e : e2;
@@ -177,6 +183,8 @@ static cudaError_t gemm_ex(const fp8imma_gemm_args* a, cudaStream_t stream) {
   p.acc_out = a->acc_out;
   p.out_bf16 = a->out_type;
   p.out_row_major = a->out_layout;
+  p.bias = t_bias;
+  p.act = t_act;
   const int group = a->a_type == FP8IMMA_A_S8 ? 16 : 8;
   if (a->act_quant == FP8IMMA_AQ_ROW) {
     if (a->M <= 0 || a->N <= 0) return cudaErrorInvalidConfiguration;
@@ -345,6 +353,16 @@ int fp8imma_launch_imma_fp8_actquant_v4_bf16(int kChunk, const void* A, const vo
 
 int fp8imma_gemm(const fp8imma_gemm_args* args, void* stream) {
   return (int)gemm_ex(args, static_cast<cudaStream_t>(stream));
+}
+
+int fp8imma_gemm_epilogue(const fp8imma_gemm_args* args, const float* bias, int act, void* stream) {
+  if (act < 0 || act > 3) return (int)cudaErrorInvalidValue;
+  t_bias = bias;
+  t_act = act;
+  const int r = fp8imma_gemm(args, stream);
+  t_bias = nullptr;
+  t_act = 0;
+  return r;
 }
 
 int fp8imma_gemm_host_io(const fp8imma_gemm_args* a, const void* A_host, void* D_host, void* stream) {

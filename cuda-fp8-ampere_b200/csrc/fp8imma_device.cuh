@@ -274,6 +274,21 @@ __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w) {
 
 // --------------------------------------------------------------- epilogue --
 
+// Optional fused epilogue after the scales, in fp32: + bias[n], then an
+// activation (0 none, 1 ReLU, 2 GELU tanh form, 3 SiLU).
+__device__ __forceinline__ float bias_act(float v, const float* bias, int n, int act) {
+  if (bias) v = __fadd_rn(v, bias[n]);  // never contracted with the scale product: round, then add
+  if (act == 1) {
+    v = fmaxf(v, 0.0f);
+  } else if (act == 2) {
+    const float u = 0.7978845608f * (v + 0.044715f * v * v * v);  // sqrt(2/pi) (v + 0.044715 v^3)
+    v = 0.5f * v * (1.0f + tanhf(u));
+  } else if (act == 3) {
+    v = v / (1.0f + expf(-v));
+  }
+  return v;
+}
+
 __device__ __forceinline__ uint16_t store_val(float v, int out_bf16) {
   return out_bf16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v)) : __half_as_ushort(__float2half_rn(v));
 }

@@ -35,6 +35,8 @@ struct GemvParams {
   float wgt_scale;                  // FMT_WGT: scale_b (or scale_b / 256 when wgt_fast)
   int wgt_fast;                     // FMT_WGT: packed decode allowed for this scale
   int no_alloc;                     // the launcher may not allocate device memory
+  const float* bias;                // optional fused epilogue: + bias[n] (fp32)
+  int act;                          // then 0 none, 1 ReLU, 2 GELU (tanh), 3 SiLU
   // column-parallel gather fused into the split-K epilogue (world > 1)
   int world, rank;
   unsigned int epoch;                       // 0: counted on the device
@@ -74,7 +76,7 @@ size_t gemm_tc_scratch_bytes(int M, int N, int K, bool native);
 cudaError_t launch_gemm_tc_s8(const GemvParams& p, int a_type, int fmt, void* scratch, cudaStream_t stream);
 cudaError_t launch_gemm_tc_fp8(const void* A, int a_type, const uint8_t* B, int b_fmt, const float* col_scale,
                                void* D, int M, int N, int K, int out_bf16, int out_row_major, void* scratch,
-                               cudaStream_t stream);
+                               cudaStream_t stream, const float* bias = nullptr, int act = 0);
 unsigned int tc_device_error(bool clear);
 cudaError_t launch_gemm_tc_wgt(const void* A_f16, const uint8_t* B, float scale_b, float* C, int M, int N, int K,
                                void* scratch, cudaStream_t stream);

@@ -128,6 +128,8 @@ struct TcParams {
   void* D;
   int32_t* acc_out;
   int out_bf16, out_row_major;
+  const float* bias;   // optional fused epilogue (bias_act)
+  int act;
   int tile_x;          // CTA-pair kernel: activation rows per tile (256, 192 or 128; MMA N)
   int n_full;          // CTA-pair kernel: tiles run at full width; the rest run as two half-width items
   uint32_t idesc_half; // instruction descriptor of the half-width items (N = tile_x / 2)
@@ -277,7 +279,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             float rs = p.row_g ? p.row_g[m < p.M ? m : 0] : 1.0f;
             v = __uint_as_float(r[j]) * rs * cs2;
           }
-          o[j] = store_val(v, p.out_bf16);
+          o[j] = store_val(bias_act(v, p.bias, n, p.act), p.out_bf16);
         }
         const int mcount = min(32, p.M - mbase);
         if (p.out_row_major) {
@@ -758,7 +760,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             float rs = p.row_g ? p.row_g[m < p.M ? m : 0] : 1.0f;
             v = __uint_as_float(r[j]) * rs * cs2;
           }
-          o[j] = store_val(v, p.out_bf16);
+          o[j] = store_val(bias_act(v, p.bias, n, p.act), p.out_bf16);
         }
         const int mcount = min(32, p.M - mbase);
         if (p.out_row_major) {
@@ -884,6 +886,7 @@ __global__ void __launch_bounds__(256) tc_splitk_reduce_kernel(const TcParams p)
       } else {
         v = sf * (p.row_g ? p.row_g[m] : 1.0f) * (p.col_scale_f32 ? p.col_scale_f32[n] : 1.0f);
       }
+      if (KIND != KIND_F16) v = bias_act(v, p.bias, n, p.act);
       if (!row_out) static_cast<uint16_t*>(p.D)[e] = store_val(v, p.out_bf16);
     }
     tile[ty + 8 * i][tx] = v;
@@ -1063,6 +1066,8 @@ cudaError_t launch_gemm_tc_s8(const GemvParams& gp, int a_type, int fmt, void* s
   p.global_scale = gp.global_scale;
   p.D = gp.D;
   p.acc_out = gp.acc_out;
+  p.bias = gp.bias;
+  p.act = gp.act;
   p.out_bf16 = gp.out_bf16;
   p.out_row_major = gp.out_row_major;
   if (g_use_pair) {
@@ -1099,7 +1104,7 @@ cudaError_t launch_quant_a_e4m3(const void* A, int a_type, int M, int K, uint8_t
 // on the raw weight bytes. b_fmt: 0 = E4M3 (hardware E4M3FN), 1 = E5M2.
 cudaError_t launch_gemm_tc_fp8(const void* A, int a_type, const uint8_t* B, int b_fmt, const float* col_scale,
                                void* D, int M, int N, int K, int out_bf16, int out_row_major, void* scratch,
-                               cudaStream_t stream) {
+                               cudaStream_t stream, const float* bias, int act) {
   uint8_t* Aq = static_cast<uint8_t*>(scratch);
   float* rs = reinterpret_cast<float*>(Aq + (((size_t)M * K + 255) & ~size_t(255)));
   if (a_type == A_BF16) launch_quant_e4m3_rows<A_BF16>(A, M, K, Aq, rs, stream);
@@ -1122,6 +1127,8 @@ cudaError_t launch_gemm_tc_fp8(const void* A, int a_type, const uint8_t* B, int 
   p.D = D;
   p.out_bf16 = out_bf16;
   p.out_row_major = out_row_major;
+  p.bias = bias;
+  p.act = act;
   if (g_use_pair) {
     p.splits = tc_pick_splits(M, N, K);
     p.ws = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(scratch) + tc_ws_offset(M, N, K, true));

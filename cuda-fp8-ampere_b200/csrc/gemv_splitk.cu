@@ -341,7 +341,7 @@ __device__ __forceinline__ void store_out(const GemvParams& p, int n, int m, int
     v = (float)sum * se;
     if (p.acc_out) p.acc_out[(size_t)n * p.M + m] = sum;
   }
-  const uint16_t o = store_val(v, p.out_bf16);
+  const uint16_t o = store_val(bias_act(v, p.bias, n, p.act), p.out_bf16);
   uint16_t* D = static_cast<uint16_t*>(p.D);
   if (p.out_row_major) {
     D[(size_t)m * p.N + n] = o;

@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(256) generic_s8_kernel(const __grid_constant__
   uint16_t sb = p.scale_tex ? tex1Dfetch<unsigned short>((cudaTextureObject_t)p.scale_tex, n) : p.scale_u16[n];
   float se = __half2float(__ushort_as_half(sb)) * (p.row_g ? p.row_g[m] : p.global_scale);
   if (p.col_scale_f32) se = se * p.col_scale_f32[n];
-  uint16_t o = store_val((float)s * se, p.out_bf16);
+  uint16_t o = store_val(bias_act((float)s * se, p.bias, n, p.act), p.out_bf16);
   uint16_t* D = static_cast<uint16_t*>(p.D);
   if (p.out_row_major) D[(size_t)m * p.N + n] = o;
   else D[(size_t)n * p.M + m] = o;

@@ -37,6 +37,7 @@ REF_SYMBOLS = [
 EXT_SYMBOLS = [
     "fp8imma_gemm",
     "fp8imma_gemm_host_io",
+    "fp8imma_gemm_epilogue",
     "fp8imma_gemm_rowquant_noalloc",
     "fp8imma_gemm_allgather",
     "fp8imma_set_fused_gather",
@@ -91,6 +92,8 @@ def lib() -> ctypes.CDLL:
     L.fp8imma_gemm.restype = I
     L.fp8imma_gemm.argtypes = [ctypes.POINTER(FP8ImmaGemmArgs), P]
     L.fp8imma_gemm_host_io.restype = I
+    L.fp8imma_gemm_epilogue.restype = I
+    L.fp8imma_gemm_epilogue.argtypes = [ctypes.POINTER(FP8ImmaGemmArgs), P, I, P]
     L.fp8imma_gemm_host_io.argtypes = [ctypes.POINTER(FP8ImmaGemmArgs), P, P, P]
     L.fp8imma_gemm_allgather.restype = I
     L.fp8imma_set_fused_gather.restype = I

@@ -75,7 +75,8 @@ std::vector<torch::Tensor> imma_fp8_gemm(torch::Tensor A, torch::Tensor B, c10::
                                          double a_inv_scale, std::string act_quant, std::string b_format,
                                          std::string path, std::string out_dtype, std::string out_layout,
                                          bool return_acc, c10::optional<torch::Tensor> out,
-                                         c10::optional<torch::Tensor> a_host, c10::optional<torch::Tensor> out_host) {
+                                         c10::optional<torch::Tensor> a_host, c10::optional<torch::Tensor> out_host,
+                                         c10::optional<torch::Tensor> bias, std::string act) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda(), "A and B must be CUDA tensors");
   TORCH_CHECK(A.is_contiguous() && B.is_contiguous(), "A and B must be contiguous");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2, "A must be [M,K] and B [N,K]");
@@ -139,6 +140,25 @@ std::vector<torch::Tensor> imma_fp8_gemm(torch::Tensor A, torch::Tensor B, c10::
   a.a_inv_scale = (float)a_inv_scale;
   a.D = D.data_ptr();
   void* stream = (void*)at::cuda::getCurrentCUDAStream();
+  int act_id = 0;
+  if (act == "none") act_id = 0;
+  else if (act == "relu") act_id = 1;
+  else if (act == "gelu") act_id = 2;
+  else if (act == "silu") act_id = 3;
+  else TORCH_CHECK(false, "act must be 'none', 'relu', 'gelu' or 'silu'");
+  if (bias.has_value() || act_id != 0) {
+    // fused epilogue: + bias[n], activation (fp8imma_gemm_epilogue)
+    TORCH_CHECK(!a_host.has_value() && !out_host.has_value(), "bias / act with host buffers is not supported");
+    const float* bp = nullptr;
+    if (bias.has_value()) {
+      auto& b = *bias;
+      TORCH_CHECK(b.is_cuda() && b.is_contiguous() && b.dim() == 1 && b.size(0) == N && b.scalar_type() == at::kFloat,
+                  "bias must be float32 [N] on CUDA");
+      bp = b.data_ptr<float>();
+    }
+    check_launch(fp8imma_gemm_epilogue(&a, bp, act_id, stream), "fp8imma_gemm_epilogue");
+    return {D, acc.defined() ? acc : torch::Tensor()};
+  }
   if (a_host.has_value() || out_host.has_value()) {
     // host-side activations in, host-side result out (fp8imma_gemm_host_io):
     // A is refreshed from a_host and D is copied to out_host on this stream
@@ -198,7 +218,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("a_inv_scale") = 1.0, py::arg("act_quant") = "tensor", py::arg("b_format") = "e4m3",
         py::arg("path") = "int8", py::arg("out_dtype") = "float16", py::arg("out_layout") = "col",
         py::arg("return_acc") = false, py::arg("out") = py::none(), py::arg("a_host") = py::none(),
-        py::arg("out_host") = py::none());
+        py::arg("out_host") = py::none(), py::arg("bias") = py::none(), py::arg("act") = "none");
   m.def("quantize_weights", &quantize_weights, "FP8 weight quantiser with per-column scales (see fp8imma_ext.h)",
         py::arg("W"), py::arg("fmt") = "e4m3");
   m.def("last_path", &last_path, "kernel family of the last call on this thread");

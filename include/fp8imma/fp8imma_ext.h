@@ -61,6 +61,11 @@ typedef struct fp8imma_gemm_args {
 // buffers (cudaMallocAsync on `stream`).
 int fp8imma_gemm(const fp8imma_gemm_args* args, void* stream);
 
+// fp8imma_gemm with a fused epilogue after the scales, in fp32 before the
+// final rounding: + bias[n] (device fp32 [N], or null), then `act`:
+// 0 none, 1 ReLU, 2 GELU (tanh form), 3 SiLU. Both paths, every kernel.
+int fp8imma_gemm_epilogue(const fp8imma_gemm_args* args, const float* bias, int act, void* stream);
+
 // fp8imma_gemm with host-side activations and result: copies A_host (M x K
 // elements of the activation type; page-locked memory for an asynchronous
 // copy) into args->A, runs fp8imma_gemm, and copies args->D (M x N outputs)

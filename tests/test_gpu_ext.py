@@ -183,3 +183,66 @@ def test_host_io_entry_matches_device_entry(cuda, M, N, K, pinned):
     with pytest.raises(RuntimeError, match="go together"):
         e.imma_fp8_gemm(a_stage, dB, ds, None, 0.5, 8.0, "tensor", "e4m3", "int8", "float16", "col", False, d_stage,
                         a_host=a_host)
+
+
+def _epilogue_ref(acc, s_u16, sig, gs, bias, act, row_g=None):
+    """Same fp32 op order as the kernels: se = cs * g (* sig); v = acc * se;
+    v += bias; activation; round to fp16."""
+    cs = s_u16.view(np.float16).astype(np.float32)
+    g = np.float32(gs) if row_g is None else row_g.astype(np.float32)[None, :]
+    se = (cs[:, None] * g).astype(np.float32)
+    if sig is not None:
+        se = (se * sig.astype(np.float32)[:, None]).astype(np.float32)
+    v = (acc.astype(np.float32) * se).astype(np.float32)
+    if bias is not None:
+        v = (v + bias.astype(np.float32)[:, None]).astype(np.float32)
+    v64 = v.astype(np.float64)
+    if act == "relu":
+        v = np.maximum(v, np.float32(0.0))
+    elif act == "gelu":
+        v = (0.5 * v64 * (1.0 + np.tanh(0.7978845608 * (v64 + 0.044715 * v64 ** 3)))).astype(np.float32)
+    elif act == "silu":
+        v = (v64 / (1.0 + np.exp(-v64))).astype(np.float32)
+    return v.astype(np.float16)
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 512, 1024), (37, 300, 256), (300, 640, 512), (128, 1024, 2048)])
+@pytest.mark.parametrize("act", ["none", "relu", "gelu", "silu"])
+def test_fused_bias_activation_epilogue(cuda, M, N, K, act):
+    """fp8imma_gemm_epilogue on the int8-exact path (split-K, tcgen05, split-K
+    tcgen05): bias and ReLU are exact in fp32, so bit-exact against the same
+    op order on the int32 accumulators; GELU / SiLU use the math library's
+    tanhf / expf, within 2 fp16 ulps."""
+    e = F.ext()
+    A, B, s, sig = inputs(M, N, K, seed=M + N)
+    bias = np.random.default_rng(1).standard_normal(N).astype(np.float32) * 0.5
+    dA = torch.from_numpy(A.view(np.int16)).cuda().view(torch.float16)
+    D, acc = e.imma_fp8_gemm(dA, torch.from_numpy(B).cuda(), torch.from_numpy(s.view(np.int16)).cuda(),
+                             torch.from_numpy(sig).cuda(), 0.05, 20.0, "tensor", "e4m3", "int8", "float16", "col", True,
+                             None, bias=torch.from_numpy(bias).cuda(), act=act)
+    torch.cuda.synchronize()
+    acc = acc.cpu().numpy()
+    ref = _epilogue_ref(acc, s, sig, np.float32(0.05), bias, act)
+    got = D.cpu().numpy()
+    if act in ("none", "relu"):
+        assert np.array_equal(got.view(np.uint16), ref.view(np.uint16))
+    else:
+        g, r = got.astype(np.float32), ref.astype(np.float32)
+        ulp = np.abs(r) * 2.0 ** -10 + 2.0 ** -24
+        assert (np.abs(g - r) <= 2 * ulp + 1e-6).all()
+
+
+@pytest.mark.parametrize("M", [16, 300])
+def test_fused_epilogue_native_path(cuda, M):
+    e = F.ext()
+    N, K = 640, 512
+    A, B, s, sig = inputs(M, N, K, seed=3)
+    bias = np.linspace(-1, 1, N).astype(np.float32)
+    dA = torch.from_numpy(A.view(np.int16)).cuda().view(torch.float16)
+    D0, _ = e.imma_fp8_gemm(dA, torch.from_numpy(B).cuda(), None, torch.from_numpy(sig).cuda(), 1.0, 1.0, "row",
+                            "e4m3", "fp8", "float16", "col", False, None)
+    D1, _ = e.imma_fp8_gemm(dA, torch.from_numpy(B).cuda(), None, torch.from_numpy(sig).cuda(), 1.0, 1.0, "row",
+                            "e4m3", "fp8", "float16", "col", False, None, bias=torch.from_numpy(bias).cuda(), act="relu")
+    torch.cuda.synchronize()
+    ref = np.maximum(D0.cpu().float().numpy() + bias[:, None], 0.0)
+    assert np.abs(D1.cpu().float().numpy() - ref).max() <= 2e-3 * np.abs(ref).max() + 1e-3
