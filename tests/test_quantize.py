@@ -76,3 +76,17 @@ def test_gpu_quantiser_feeds_the_gemm(cuda):
     _, D_o, _ = O.imma_fp8("v4_f16", 32, A.view(np.uint16), B.cpu().numpy(), st.cpu().numpy().view(np.uint16),
                            0.25, 4.0)
     assert bits_equal(to_np_bits(D), D_o).all()
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_oracle_decoders_match_torch_on_all_codes(fmt):
+    codes = np.arange(256, dtype=np.uint8)
+    t = torch.from_numpy(codes).view(torch.float8_e4m3fn if fmt == "e4m3" else torch.float8_e5m2).float().numpy()
+    o = O.e4m3fn_decode(codes) if fmt == "e4m3" else O.e5m2_decode(codes)
+    nan = np.isnan(t)
+    assert (np.isnan(o) == nan).all()
+    assert np.array_equal(o[~nan], t[~nan])
+    # encode(decode(b)) == b for every finite code (satfinite encoders map +-Inf to the largest finite)
+    fin = np.isfinite(o)
+    enc = O.e4m3fn_encode(o[fin]) if fmt == "e4m3" else O.e5m2_encode(o[fin])
+    assert np.array_equal(enc, codes[fin])
