@@ -26,8 +26,14 @@
 //     half of each K chunk of B stale there).
 #pragma once
 
+#ifdef __cplusplus
 #include <cstddef>
 #include <cstdint>
+#else
+/* plain C callers (FFI bindings, cgo) see only the C ABI below */
+#include <stddef.h>
+#include <stdint.h>
+#endif
 
 #ifdef __CUDACC__
 #include <cuda_bf16.h>
@@ -35,6 +41,7 @@
 #include <cuda_runtime.h>
 #endif
 
+#ifdef __cplusplus
 namespace fp8imma {
 
 // reference imma_fp8.h:23
@@ -91,6 +98,7 @@ cudaError_t launch_imma_fp8_actquant_v4_texscale_bf16(int kChunk, const __nv_bfl
 #endif
 
 }  // namespace fp8imma
+#endif  // __cplusplus
 
 #ifdef __cplusplus
 extern "C" {
