@@ -70,3 +70,29 @@ def test_torch_ext_rejects_cpu_tensors():
     s = torch.zeros(16, dtype=torch.float16)
     with pytest.raises(RuntimeError, match="A must be a CUDA tensor"):
         e.imma_fp8_v4_act(A, B, s, 1.0, 1.0, 32)
+
+
+def test_extension_entries_reject_bad_arguments_before_any_launch():
+    """Host-side validation of the extension entry points and tuning knobs:
+    these return the CUDA error code without touching a device, so they run
+    here."""
+    import ctypes
+
+    import fp8imma_b200 as F
+
+    L = F.lib()
+    INVALID_VALUE, INVALID_CONFIG = 1, 9
+    p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    assert L.fp8imma_quantize_weights(p, 0, 0, 16, 0, p, None, None, None) == INVALID_CONFIG
+    assert L.fp8imma_quantize_weights(None, 0, 4, 16, 0, p, None, None, None) == INVALID_VALUE
+    assert L.fp8imma_quantize_weights(p, 3, 4, 16, 0, p, None, None, None) == INVALID_VALUE
+    assert L.fp8imma_quantize_weights(p, 0, 4, 16, 3, p, None, None, None) == INVALID_VALUE
+    a = F.FP8ImmaGemmArgs()
+    assert L.fp8imma_gemm_epilogue(ctypes.byref(a), None, 4, None) == INVALID_VALUE
+    assert L.fp8imma_gemm_epilogue(ctypes.byref(a), None, -1, None) == INVALID_VALUE
+    assert L.fp8imma_gemm_host_io(ctypes.byref(a), None, None, None) == INVALID_VALUE
+    for setter, bad, good in [(L.fp8imma_set_stream_k, 3, 1), (L.fp8imma_set_tc_splitk, 0, -1),
+                              (L.fp8imma_set_tc_tile_x, 100, 0), (L.fp8imma_set_fused_gather, 2, 0),
+                              (L.fp8imma_set_tc_half_tail, 2, 1), (L.fp8imma_set_splitk, 3, 0)]:
+        assert setter(bad) == INVALID_VALUE
+        assert setter(good) == 0
