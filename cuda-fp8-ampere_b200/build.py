@@ -27,7 +27,7 @@ LIB = os.path.join(HERE, "libfp8imma.so")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
+NVCC_FLAGS = ["-DFP8IMMA_NVTX", "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
               "--expt-relaxed-constexpr", "-I" + INCLUDE, "-I" + CSRC]
 
 CU_SOURCES = ["api.cu", "gemv_splitk.cu", "generic.cu", "fp8wgt.cu", "host_util.cu", "gemm_tc.cu", "noalloc.cu", "peer.cu", "quantize.cu"]

@@ -8,6 +8,7 @@
 #include "fp8imma/fp8imma_ext.h"
 #include "fp8imma/imma_fp8.h"
 #include "fp8imma_kernels.h"
+#include "nvtx_range.h"
 
 #include <algorithm>
 #include <atomic>
@@ -111,6 +112,7 @@ static GemvParams base_params(const void* A, const void* B, const void* scales, 
 static int ref_launch(int kChunk, int a_type, int group, const void* A, const void* B, const void* scales,
                       unsigned long long tex, void* D, int M, int N, int K, float gs, float ainv,
                       void* stream) {
+  FP8IMMA_RANGE("fp8imma reference launcher");
   if (kChunk != 32 && kChunk != 64) return (int)cudaErrorInvalidValue;
   GemvParams p = base_params(A, B, scales, tex, D, M, N, K, gs, ainv);
   return (int)run_int8(p, a_type, FMT_E4M3_REF, group, static_cast<cudaStream_t>(stream));
@@ -352,6 +354,7 @@ int fp8imma_launch_imma_fp8_actquant_v4_bf16(int kChunk, const void* A, const vo
 }
 
 int fp8imma_gemm(const fp8imma_gemm_args* args, void* stream) {
+  FP8IMMA_RANGE("fp8imma_gemm");
   return (int)gemm_ex(args, static_cast<cudaStream_t>(stream));
 }
 
@@ -366,6 +369,7 @@ int fp8imma_gemm_epilogue(const fp8imma_gemm_args* args, const float* bias, int 
 }
 
 int fp8imma_gemm_host_io(const fp8imma_gemm_args* a, const void* A_host, void* D_host, void* stream) {
+  FP8IMMA_RANGE("fp8imma_gemm_host_io");
   if (!a || !A_host || !D_host || !a->A || !a->D || a->M <= 0 || a->N <= 0 || a->K <= 0)
     return (int)cudaErrorInvalidValue;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

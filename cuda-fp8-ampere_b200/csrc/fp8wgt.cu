@@ -12,6 +12,7 @@
 #include "fp8imma/fp8imma_ext.h"
 #include "fp8imma_device.cuh"
 #include "fp8imma_kernels.h"
+#include "nvtx_range.h"
 
 using namespace fp8imma_dev;
 
@@ -105,6 +106,7 @@ __global__ void __launch_bounds__(kWThreads) fp8wgt_kernel(const uint16_t* __res
 
 extern "C" int fp8imma_fp8wgt_linear_forward(const void* A, const void* B, float scale_b, void* C, int M,
                                              int N, int K, void* stream) {
+  FP8IMMA_RANGE("fp8imma_fp8wgt_linear_forward");
   using namespace fp8imma_b200;
   if (M <= 0 || N <= 0) return (int)cudaErrorInvalidConfiguration;
   if (!A || !B || !C || K <= 0 || (K % 16) != 0) return (int)cudaErrorInvalidValue;

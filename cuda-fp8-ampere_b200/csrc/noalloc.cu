@@ -13,6 +13,7 @@
 // that loads this library holds until the process exits.
 #include "fp8imma/fp8imma_ext.h"
 #include "fp8imma_kernels.h"
+#include "nvtx_range.h"
 
 #include <mutex>
 
@@ -55,6 +56,7 @@ cudaError_t scratch_for_current_device(void** out) {
 using namespace fp8imma_b200;
 
 extern "C" int fp8imma_gemm_rowquant_noalloc(const fp8imma_gemm_args* a, void* stream) {
+  FP8IMMA_RANGE("fp8imma_gemm_rowquant_noalloc");
   if (!a) return (int)cudaErrorInvalidValue;
   if (a->path != FP8IMMA_PATH_INT8_EXACT || a->act_quant != FP8IMMA_AQ_ROW) return (int)cudaErrorInvalidValue;
   if (a->a_type != FP8IMMA_A_F16 && a->a_type != FP8IMMA_A_BF16) return (int)cudaErrorInvalidValue;

@@ -11,6 +11,7 @@
 // NCCL). Waits are bounded: on timeout a code is recorded and the kernel ends.
 #include "fp8imma/fp8imma_ext.h"
 #include "fp8imma_kernels.h"
+#include "nvtx_range.h"
 
 #include <cuda_fp16.h>
 
@@ -135,6 +136,7 @@ extern "C" int fp8imma_set_fused_gather(int enable) {
 
 extern "C" int fp8imma_gemm_allgather(const fp8imma_gemm_args* a, void* const* peer_out, void* const* peer_signal,
                                       int world, int rank, unsigned int epoch, void* stream) {
+  FP8IMMA_RANGE("fp8imma_gemm_allgather");
   if (!a || !peer_out || !peer_signal || world < 1 || world > 8 || rank < 0 || rank >= world)
     return (int)cudaErrorInvalidValue;
   if (a->path != FP8IMMA_PATH_INT8_EXACT || a->act_quant != FP8IMMA_AQ_TENSOR || a->out_layout != FP8IMMA_OUT_COL)

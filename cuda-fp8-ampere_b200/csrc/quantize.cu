@@ -13,6 +13,7 @@
 // definition describes. Weights must be finite.
 #include "fp8imma/fp8imma_ext.h"
 #include "fp8imma_kernels.h"
+#include "nvtx_range.h"
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -97,6 +98,7 @@ using namespace fp8imma_b200;
 
 extern "C" int fp8imma_quantize_weights(const void* W, int w_type, int N, int K, int fmt, void* B_out,
                                         float* col_scale_out, uint16_t* step_out, void* stream) {
+  FP8IMMA_RANGE("fp8imma_quantize_weights");
   if (N <= 0 || K <= 0) return (int)cudaErrorInvalidConfiguration;
   if (!W || !B_out || w_type < 0 || w_type > 2 || fmt < 0 || fmt > 2) return (int)cudaErrorInvalidValue;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
