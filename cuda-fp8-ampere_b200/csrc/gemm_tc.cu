@@ -812,31 +812,17 @@ bool g_use_pair = true;
 int g_tc_splitk = -1;  // -1 automatic, else forced K splits of the CTA-pair kernel
 int g_tc_tile_x = 0;   // 0 automatic, else forced activation rows per tile (256, 192, 128)
 bool g_tc_half_tail = true;  // run the last partial round of tiles as half-width items
-bool g_tc_tile_model = false;  // the rounds model below is kept for reference, not used
 
-// Activation rows per CTA-pair tile. Tiles are dealt round-robin to the CTA
-// pairs, so the last round can run mostly empty (4096^2: 256 tiles of 256 on
-// 74 pairs = 3.46 rounds). Narrower tiles balance the rounds but cost more
-// operand traffic per MAC; measured (4096^2, 2048x11008x4096, 8192^3,
-// 4096x28672x8192) 192 and 128 were 5-60% slower than 256 everywhere, so 256
-// is used unless forced. (Model: minimise rounds x (rows + 64).)
+// Activation rows per CTA-pair tile (the MMA's N). 256 unless forced: 192 and
+// 128 balance the rounds of tiles over the CTA pairs better (4096^2: 256
+// tiles of 256 on 74 pairs = 3.46 rounds) but cost more operand traffic per
+// MAC, and measured 5-60% slower on 4096^2, 2048x11008x4096, 8192^3 and
+// 4096x28672x8192; the last partial round is handled by half-width items
+// instead (n_full in launch_tc2).
 int tc_pick_tile_x(int M, int N) {
-  if (g_tc_tile_x) return g_tc_tile_x;
-  if (!g_tc_tile_model) return 256;  // measured: narrower tiles were slower on every shape tried
-  const int pairs = num_sms_current() / 2;
-  const int tw = (N + 255) / 256;
-  int best = 256;
-  long long best_cost = -1;
-  for (int t : {256, 192, 128}) {
-    const long long tiles = (long long)tw * ((M + t - 1) / t);
-    const long long rounds = (tiles + pairs - 1) / pairs;
-    const long long cost = rounds * (t + 64);
-    if (best_cost < 0 || cost < best_cost) {
-      best_cost = cost;
-      best = t;
-    }
-  }
-  return best;
+  (void)M;
+  (void)N;
+  return g_tc_tile_x ? g_tc_tile_x : 256;
 }
 
 // Split-K finish: sum the raw accumulators of the K splits in a fixed order
