@@ -5,10 +5,16 @@
 // (wmma_fp16a_fp8e4m3b_gemm_kernel_tiled_vec4 + fp8_linear_forward):
 //   Bdec[n,k] = fp16_rn( float(lut[B[n,k]]) * scale_b )
 //   C[m,n]    = sum_k A[m,k] * Bdec[n,k]        (fp32 accumulation)
-// Here: one warp per 16 weight columns x 8*MB rows of A, weights streamed with
-// 128-bit loads, decoded in registers and fed to mma.sync m16n8k16 f16 (the
-// decoded fp16 weights form the MMA's A operand, the activations its B
-// operand), K split across the 8 warps of a CTA and reduced in shared memory.
+// Routing (fp8imma_fp8wgt_linear_forward):
+//   * M > 64, 16-byte aligned weights: one pass decodes the weights to fp16
+//     scratch, then the CTA-pair tcgen05 GEMM with kind::f16 (gemm_tc.cu);
+//   * M <= 64, 16-byte aligned weights: the fp16 mode (FMT_WGT) of the TMA
+//     split-K kernel (gemv_splitk.cu), weights decoded in registers;
+//   * otherwise (8-byte aligned weights) fp8wgt_kernel below: one warp per 16
+//     weight columns x 8*MB rows of A, weights streamed with 64-bit loads,
+//     decoded in registers and fed to mma.sync m16n8k16 f16 (the decoded fp16
+//     weights form the MMA's A operand, the activations its B operand), K
+//     split across the 8 warps of a CTA and reduced in shared memory.
 #include "fp8imma/fp8imma_ext.h"
 #include "fp8imma_device.cuh"
 #include "fp8imma_kernels.h"
