@@ -1,4 +1,4 @@
-// Split-K skinny GEMM for small M (decode shapes), reference-exact int8 path.
+// Split-K skinny GEMM for small M (decode shapes).
 //
 // Work split (B200):
 //   * a CTA owns 128 weight columns and one K-slice; the K-slices of a column
@@ -17,6 +17,14 @@
 // through sigma(g) = (g>>1) + 4*(g&1), which puts the two rows read by one
 // 8-lane shared-memory phase in different halves of the 128-byte swizzle
 // pattern (conflict-free).
+//
+// Modes (FMT): reference-exact int8 (E4M3 table / E5M2 weights transcoded
+// in registers, m16n8k32 s8), native FP8 (weight bytes and E4M3 activations
+// straight into m16n8k32 e4m3/e5m2 with fp32 accumulation) and the fp8wgt
+// fp16 mode (weights decoded to fp16(lut * scale), m16n8k16 f16, fp32 output).
+// Two forms: the cluster kernel above (default), and a stream-K kernel
+// (persistent CTAs, an even share of 64-wide K halves each, partial tiles
+// finished by the last arriving CTA) for large projections.
 //
 // Reference counterpart: imma_gemm_fp8_actquant_cpasync_int8_colscale_fp16_
 // colmajor_kernel_v4 (src/fp8imma/impl/v4_kernels.inl:1-287), v3
