@@ -22,7 +22,7 @@
 // in registers, m16n8k32 s8), native FP8 (weight bytes and E4M3 activations
 // straight into m16n8k32 e4m3/e5m2 with fp32 accumulation) and the fp8wgt
 // fp16 mode (weights decoded to fp16(lut * scale), m16n8k16 f16, fp32 output).
-// Two forms: the cluster kernel above (default), and a stream-K kernel
+// Two forms: the cluster form described above (default), and a stream-K kernel
 // (persistent CTAs, an even share of 64-wide K halves each, partial tiles
 // finished by the last arriving CTA) for large projections.
 //
