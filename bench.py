@@ -201,7 +201,7 @@ def main():
     ap.add_argument("--no-ref-lib", action="store_true")
     ap.add_argument("--points", action="store_true", help="also time the other decode/70B shapes")
     ap.add_argument("--points-only", default="", help="comma-separated subset of the --points shapes")
-    ap.add_argument("--pdl", action="store_true", help="launch with programmatic dependent launch")
+    ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--gather", default="peer", choices=["peer", "peer-epilogue", "nccl"],
                     help="N>1: NVLink gather in a kernel after the GEMM (peer), in the GEMM's epilogue "
                          "(peer-epilogue), or NCCL all-gather")
@@ -227,7 +227,7 @@ def main():
     from fp8imma_b200 import workloads as WL
 
     ext = F.ext()
-    F.lib().fp8imma_set_pdl(1 if args.pdl else 0)
+    F.lib().fp8imma_set_pdl(0 if args.no_pdl else 1)
     M, Nl, K = w["M"], w["N"], w["K"]
     N_tot = Nl * world
     B, s16, sig = WL.make_weights(Nl, K, w["sigma_w"], "e4m3", seed=rank, device="cuda")
@@ -445,7 +445,7 @@ def main():
                        "path": "int8-exact (reference v4 semantics)", "parallelism": "column-parallel x%d" % world,
                        "l2": "weights rotated over %d copies (%.0f MB > 2x L2)" % (copies, copies * wbytes / 1e6),
                        "timing": timing,
-                       "pdl": bool(args.pdl)},
+                       "pdl": not args.no_pdl},
             "tflops": round(tflops, 4),
             "roofline": dict(roof, traffic=traffic),
             "cpu_baseline": cpu,

@@ -30,7 +30,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-DFP8IMMA_NVTX", "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
               "--expt-relaxed-constexpr", "-I" + INCLUDE, "-I" + CSRC]
 
-CU_SOURCES = ["api.cu", "gemv_splitk.cu", "generic.cu", "fp8wgt.cu", "host_util.cu", "gemm_tc.cu", "noalloc.cu", "peer.cu", "quantize.cu"]
+CU_SOURCES = ["api.cu", "gemv_splitk.cu", "decode.cu", "generic.cu", "fp8wgt.cu", "host_util.cu", "gemm_tc.cu", "noalloc.cu", "peer.cu", "quantize.cu"]
 
 
 def _run(cmd: list[str]) -> None:

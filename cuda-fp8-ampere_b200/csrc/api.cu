@@ -21,10 +21,11 @@ namespace fp8imma_b200 {
 namespace {
 std::atomic<int> g_splitk{0};
 std::atomic<int> g_small_m_max{64};
-std::atomic<int> g_pdl{0};
+std::atomic<int> g_pdl{1};
 thread_local int t_last_path = 0;
 #ifdef FP8IMMA_TRACE
 unsigned long long* g_trace = nullptr;  // trace builds only
+int g_dbg = 0;
 #endif
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -73,6 +74,7 @@ static cudaError_t run_int8(GemvParams p, int a_type, int fmt, int group, cudaSt
   p.pdl = g_pdl.load();
 #ifdef FP8IMMA_TRACE
   p.trace = g_trace;
+  p.dbg = g_dbg;
 #endif
   const bool fast_shape = p.K > 0 && (p.K % 16) == 0 && aligned16(p.A) && aligned16(p.B);
   if (fast_shape && p.M > g_small_m_max.load()) {
@@ -85,8 +87,9 @@ static cudaError_t run_int8(GemvParams p, int a_type, int fmt, int group, cudaSt
     return e != cudaSuccess ? e : e2;
   }
   if (fast_shape) {
-    t_last_path = 1;
-    return launch_gemv_s8(p, a_type, fmt, g_splitk.load(), stream);
+    const cudaError_t e = launch_gemv_s8(p, a_type, fmt, g_splitk.load(), stream);
+    t_last_path = gemv_last_used_decode() ? 6 : 1;
+    return e;
   }
   t_last_path = 2;
   return launch_generic_s8(p, a_type, fmt, stream);
@@ -306,6 +309,7 @@ extern "C" {
 
 #ifdef FP8IMMA_TRACE
 void fp8imma_debug_set_trace(void* buf) { g_trace = static_cast<unsigned long long*>(buf); }
+void fp8imma_debug_set_mode(int m) { g_dbg = m; }
 #endif
 
 void fp8imma_init_fp8_e4m3_lut(void) { fp8imma::init_fp8_e4m3_lut(); }
@@ -425,13 +429,29 @@ int fp8imma_set_tc_pair(int enable) {
   return 0;
 }
 
+int fp8imma_set_decode_kernel(int enable) {
+  if (enable != 0 && enable != 1) return (int)cudaErrorInvalidValue;
+  decode_set_mode(enable);
+  return 0;
+}
+
 int fp8imma_set_pdl(int enable) {
   g_pdl.store(enable ? 1 : 0);
   return 0;
 }
 
 unsigned int fp8imma_device_error(int clear) {
-  return gemv_device_error(clear != 0) | tc_device_error(clear != 0) | peer_device_error(clear != 0);
+  return gemv_device_error(clear != 0) | decode_device_error(clear != 0) | tc_device_error(clear != 0) |
+         peer_device_error(clear != 0);
+}
+
+int fp8imma_set_wait_limit_ns(unsigned long long ns) {
+  if (ns == 0) return (int)cudaErrorInvalidValue;
+  cudaError_t e = gemv_set_wait_limit(ns);
+  if (e == cudaSuccess) e = decode_set_wait_limit(ns);
+  if (e == cudaSuccess) e = tc_set_wait_limit(ns);
+  if (e == cudaSuccess) e = peer_set_wait_limit(ns);
+  return (int)e;
 }
 
 const char* fp8imma_version(void) { return "fp8imma-b200 0.1 (sm_100a)"; }

@@ -1,0 +1,598 @@
+// Balanced decode-shape GEMM (M <= 16, int8-exact path): one CTA per SM.
+//
+// The weight matrix is cut into 8-column groups. A cluster of S CTAs (S = 1,
+// or a pair on one TPC, S = 2) owns a contiguous run of G groups (G differs by
+// at most one between clusters, so every SM streams the same number of
+// weight bytes to within one group); the S CTAs of the cluster split K. The
+// grid is a single wave of at most one CTA per SM.
+//
+// Inside a CTA (2*G consumer warps + one TMA producer warp):
+//   * the producer requests a few weight stages (8G rows x 128 K-bytes, one
+//     2-D TMA box with 128-byte swizzle), then the CTA's activation rows (one
+//     2-D TMA box of up to 16 rows x 128 bytes each, issued after the previous
+//     kernel has finished when launched with programmatic dependent launch),
+//     then the rest of the weight stages: at decode sizes the ring holds the
+//     whole K-slice, so every byte of the call is requested at once;
+//   * the consumers quantise the activation rows from shared memory into an
+//     int8 copy (row stride = 64 mod 128 bytes: conflict-free fragment loads);
+//   * consumer warp (c, q) owns group c and every stage i = q (mod 2): two
+//     16-byte conflict-free shared loads of its column's 128 bytes, the FP8 ->
+//     int8 transcode in registers, and four mma.sync m16n8k32 s8 with the
+//     weights as the B operand (8 columns) and the activation rows as the A
+//     operand (16 rows), into four independent accumulator sets;
+//   * the two warps of a group add their fragments through shared memory;
+//     with S = 2 each CTA owns the epilogue of half of the groups and pushes
+//     the other half's sums into its peer's shared memory with st.async,
+//     completing on the peer's mbarrier (no cluster-wide barrier at the end).
+// K order inside each 64-byte half is permuted identically for both operands
+// (int32 sums do not depend on order). Lane group g reads weight column
+// sigma(g) = (g>>1) + 4(g&1) of its group, which makes each 8-lane shared
+// memory phase conflict-free under the 128-byte swizzle.
+//
+// Semantics (every rounding step) are those of the reference v4 kernel,
+// src/fp8imma/impl/v4_kernels.inl:61-70 (weight transcode), 116-131
+// (activation quantisation) and 280-285 (epilogue); the arithmetic helpers
+// live in fp8imma_device.cuh.
+#include "fp8imma_device.cuh"
+#include "fp8imma_kernels.h"
+#include "sm100_async.cuh"
+
+#include <atomic>
+
+using namespace fp8imma_dev;
+
+namespace fp8imma_b200 {
+
+namespace {
+
+#ifndef DEC_WPG
+#define DEC_WPG 2
+#endif
+constexpr int kDecMaxG = 8;        // 8-column groups per CTA
+constexpr int kDecWpg = DEC_WPG;   // consumer warps per group (stage i goes to warp i mod kDecWpg)
+constexpr int kDecBoxK = 128;      // K bytes per weight stage
+constexpr int kDecMaxStages = 16;
+constexpr int kDecMaxThreads = kDecMaxG * kDecWpg * 32 + 32;
+constexpr int kDecEarlyStages = 4;  // weight stages requested before the activations
+constexpr int kDecRows = 16;        // activation rows (one m16 block)
+constexpr int kDecABox = 128;       // activation bytes per row per TMA box
+
+struct DecodeCfg {
+  int S;            // CTAs per cluster (K split)
+  int P;            // clusters
+  int NG;           // 8-column groups in N
+  int gmax;         // groups of the widest cluster
+  int D;            // stage ring depth
+  int kper;         // K per CTA (multiple of kDecBoxK)
+  int astride;      // int8 activation row stride in shared memory (kper + 64)
+  int stage_bytes;  // gmax * 1024
+  int arows;        // activation rows moved per box (min(M, 16))
+  int off_bar, off_const, off_raw, off_aq, off_tot, off_recv;
+};
+
+#ifdef FP8IMMA_TRACE
+// per CTA 64 words: [0] %globaltimer at entry, [1] SM id, [2, 16) clock64
+// cycles since entry at point i
+#define DEC_TRACE(i)                                                                                  \
+  do {                                                                                                \
+    if (p.trace && threadIdx.x == 0) p.trace[(size_t)blockIdx.x * 64 + (i)] = clock64() - trace_clk0; \
+  } while (0)
+#else
+#define DEC_TRACE(i) do { } while (0)
+#endif
+
+__device__ __forceinline__ void dec_mma(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 dec_lds128(uint32_t addr) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr));
+  return r;
+}
+
+__device__ __forceinline__ uint16_t dec_scale_bits(const GemvParams& p, int n) {
+  if (p.scale_tex) return tex1Dfetch<unsigned short>((cudaTextureObject_t)p.scale_tex, n);
+  return p.scale_u16[n];
+}
+
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_to_rank(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+// 8-byte store into another CTA's shared memory, counted on its mbarrier
+__device__ __forceinline__ void st_async_v2(uint32_t remote_addr, int a, int b, uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.s32 [%0], {%1, %2}, [%3];" ::"r"(remote_addr), "r"(a),
+      "r"(b), "r"(remote_bar)
+      : "memory");
+}
+
+// Bounded mbarrier wait with the first probe inline and the polling loop out
+// of line (keeps the hot loop small).
+__device__ __noinline__ bool dec_wait_slow(uint64_t* bar, uint32_t parity, unsigned int err) {
+  return mbar_wait(bar, parity, err);
+}
+__device__ __forceinline__ bool dec_wait(uint64_t* bar, uint32_t parity, unsigned int err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return dec_wait_slow(bar, parity, err);
+}
+
+template <int FMT, bool FAST>
+__device__ __forceinline__ uint32_t dec_tc4(uint32_t x, uint32_t fscale, uint16_t inv_h) {
+  if (FAST) return FMT == FMT_E5M2 ? transcode4_fast_e5m2(x, fscale) : transcode4_fast_e4m3(x, fscale);
+  return transcode4_exact<FMT>(x, inv_h);
+}
+
+// Activation rows (TMA-staged, `raw`: box j = [arows][128 bytes] at j * 2048)
+// -> int8 rows of `aq` (row stride astride), reference rounding. One item is
+// 16 raw bytes: 8 fp16/bf16 values or 16 int8 values.
+template <int AT>
+__device__ __forceinline__ void dec_quant_rows(const uint8_t* raw, int8_t* aq, int astride, int nbox, int arows,
+                                               const uint16_t* rowinv_s, int tid, int nthr) {
+  const int per_box = arows * 8;
+  const int total = nbox * per_box;
+  // item it = jb * per_box + rem, advanced without divisions
+  const int djb = nthr / per_box, drem = nthr - djb * per_box;
+  int jb = tid / per_box, rem = tid - jb * per_box;
+  for (int it = tid; it < total; it += nthr) {
+    const int r = rem >> 3, c = rem & 7;
+    const uint4 v = *reinterpret_cast<const uint4*>(raw + (size_t)jb * (kDecRows * kDecABox) + rem * 16);
+    if (AT == A_S8) {
+      *reinterpret_cast<uint4*>(aq + r * astride + jb * kDecABox + c * 16) = v;
+    } else {
+      const uint16_t ainv = rowinv_s[r];
+      const uint32_t ainv2 = (uint32_t)ainv | ((uint32_t)ainv << 16);
+      uint4 w = v;
+      if (AT == A_BF16) {
+        w.x = bf16x2_to_f16x2(w.x);
+        w.y = bf16x2_to_f16x2(w.y);
+        w.z = bf16x2_to_f16x2(w.z);
+        w.w = bf16x2_to_f16x2(w.w);
+      }
+      *reinterpret_cast<uint2*>(aq + r * astride + jb * (kDecABox / 2) + c * 8) =
+          make_uint2(quant4_f16(w.x, w.y, ainv2), quant4_f16(w.z, w.w, ainv2));
+    }
+    jb += djb;
+    rem += drem;
+    if (rem >= per_box) {
+      rem -= per_box;
+      ++jb;
+    }
+  }
+}
+
+// One element of the epilogue from its int32 sum: scales in the reference's
+// order, optional bias/activation, cast, store (col-major or row-major).
+__device__ __forceinline__ void dec_store(const GemvParams& p, int n, int m, int32_t sum, float sc, float cs,
+                                          float rg) {
+  float se = sc * rg;
+  if (p.col_scale_f32) se = se * cs;
+  const float v = (float)sum * se;
+  if (p.acc_out) p.acc_out[(size_t)n * p.M + m] = sum;
+  const uint16_t o = store_val(bias_act(v, p.bias, n, p.act), p.out_bf16);
+  uint16_t* D = static_cast<uint16_t*>(p.D);
+  if (p.out_row_major)
+    D[(size_t)m * p.N + n] = o;
+  else
+    D[(size_t)n * p.M + m] = o;
+}
+
+// One stage of a consumer warp: this lane's 2 x 16 weight bytes, eight
+// transcodes, four MMAs into four accumulator sets.
+template <int FMT, bool FAST>
+__device__ __forceinline__ void dec_stage(int (&acc)[2][2][4], uint32_t w_addr, uint32_t a_addr, int astride,
+                                          bool hi_rows, uint32_t fs, uint16_t inv, int sw0, int sw1) {
+  const uint4 w0 = dec_lds128(w_addr + sw0);
+  const uint4 w1 = dec_lds128(w_addr + sw1);
+  uint32_t b[2][4];
+  b[0][0] = dec_tc4<FMT, FAST>(w0.x, fs, inv);
+  b[0][1] = dec_tc4<FMT, FAST>(w0.y, fs, inv);
+  b[0][2] = dec_tc4<FMT, FAST>(w0.z, fs, inv);
+  b[0][3] = dec_tc4<FMT, FAST>(w0.w, fs, inv);
+  b[1][0] = dec_tc4<FMT, FAST>(w1.x, fs, inv);
+  b[1][1] = dec_tc4<FMT, FAST>(w1.y, fs, inv);
+  b[1][2] = dec_tc4<FMT, FAST>(w1.z, fs, inv);
+  b[1][3] = dec_tc4<FMT, FAST>(w1.w, fs, inv);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint4 x = dec_lds128(a_addr + 64 * h);
+    uint4 y = make_uint4(0u, 0u, 0u, 0u);
+    if (hi_rows) y = dec_lds128(a_addr + 8 * astride + 64 * h);
+    dec_mma(acc[h][0], x.x, y.x, x.y, y.y, b[h][0], b[h][1]);
+    dec_mma(acc[h][1], x.z, y.z, x.w, y.w, b[h][2], b[h][3]);
+  }
+}
+
+template <int FMT, bool FAST, int W>
+__device__ __forceinline__ bool dec_loop(int (&acc)[2][2][4], uint32_t stages_a, uint64_t* full, uint64_t* empty,
+                                         uint32_t aq_a, int astride, int stage_bytes, int D, int nst, int c, int q,
+                                         int lane, bool hi_rows, uint32_t fs, uint16_t inv) {
+  const int g = lane >> 2, t = lane & 3;
+  const int sg = (g >> 1) + 4 * (g & 1);
+  const uint32_t wrow = stages_a + (8 * c + sg) * kDecBoxK;
+  const int sw0 = (t ^ sg) << 4, sw1 = ((4 + t) ^ sg) << 4;  // 16-byte chunks of halves 0 and 1 (swizzled)
+  uint32_t a_addr = aq_a + g * astride + 16 * t + q * kDecBoxK;
+  bool ok = true;
+  int s = q;
+  uint32_t phase = 0;
+  for (int i = q; i < nst; i += W) {
+    if (ok) ok = dec_wait(&full[s], phase, ERR_WAIT_FULL);
+    dec_stage<FMT, FAST>(acc, wrow + s * stage_bytes, a_addr, astride, hi_rows, fs, inv, sw0, sw1);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    a_addr += W * kDecBoxK;
+    s += W;
+    if (s >= D) {
+      s -= D;
+      phase ^= 1u;
+    }
+  }
+  return ok;
+}
+
+template <int AT, int FMT>
+__global__ void __launch_bounds__(kDecMaxThreads, 1)
+    decode_kernel(const __grid_constant__ GemvParams p, const __grid_constant__ CUtensorMap tm_full,
+                  const __grid_constant__ CUtensorMap tm_short, const __grid_constant__ CUtensorMap tm_act,
+                  const __grid_constant__ DecodeCfg cfg) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+#ifdef FP8IMMA_TRACE
+  const long long trace_clk0 = clock64();
+  if (p.trace && threadIdx.x == 0) {
+    unsigned int sm_;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm_));
+    p.trace[(size_t)blockIdx.x * 64 + 0] = globaltimer_ns();
+    p.trace[(size_t)blockIdx.x * 64 + 1] = sm_;
+  }
+#endif
+  uint8_t* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + cfg.off_bar);
+  uint64_t* empty = full + kDecMaxStages;
+  uint64_t* recv_bar = empty + kDecMaxStages;
+  uint64_t* act_bar = recv_bar + 1;
+  float* sc_s = reinterpret_cast<float*>(smem + cfg.off_const);  // [64] column int8 steps (fp32)
+  float* cs_s = sc_s + 64;                                       // [64] fp32 column multipliers
+  float* rg_s = cs_s + 64;                                       // [16] per-row global scales
+  uint16_t* rowinv_s = reinterpret_cast<uint16_t*>(rg_s + 16);   // [16] per-row activation multipliers
+  uint8_t* raw = smem + cfg.off_raw;
+  int8_t* aq = reinterpret_cast<int8_t*>(smem + cfg.off_aq);
+  int32_t* tot = reinterpret_cast<int32_t*>(smem + cfg.off_tot);    // [gmax][wpg][16][8] own sums, parking
+  int32_t* recv = reinterpret_cast<int32_t*>(smem + cfg.off_recv);  // [gmax][16][8] the peer's sums
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nthr = blockDim.x - 32;  // consumer threads
+  const int cwarps = nthr >> 5;
+  const int S = cfg.S;
+  const int rank = S > 1 ? (int)cluster_ctarank() : 0;
+  const int pc = blockIdx.x / S;
+  const int cg0 = (int)((long long)pc * cfg.NG / cfg.P);
+  const int G = (int)((long long)(pc + 1) * cfg.NG / cfg.P) - cg0;
+  const int n0 = cg0 * 8;
+  const int k0 = rank * cfg.kper;
+  const int k1 = min(p.K, k0 + cfg.kper);
+  const int nst = k1 > k0 ? (k1 - k0 + kDecBoxK - 1) / kDecBoxK : 0;
+  const int esz = AT == A_S8 ? 1 : 2;
+  const int abox_k = kDecABox / esz;  // activation K elements per box
+  const int nbox = k1 > k0 ? (k1 - k0 + abox_k - 1) / abox_k : 0;
+  const int gh = (G + 1) >> 1;  // groups [0, gh) finish on rank 0, [gh, G) on rank 1
+  const int own_lo = rank == 0 ? 0 : gh, own_hi = (S == 1 || rank == 1) ? G : gh;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < cfg.D; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], G);
+    }
+    mbar_init(recv_bar, 1);
+    mbar_init(act_bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (S > 1) {
+    cluster_arrive_release();  // publishes the barrier initialisation to the peer
+    if (threadIdx.x == 0) mbar_arrive_expect_tx(recv_bar, (uint32_t)((own_hi - own_lo) * kDecRows * 8 * 4));
+  }
+  if (p.pdl) pdl_launch_dependents();  // the next grid may take SMs as this one's CTAs exit
+  DEC_TRACE(2);
+
+  const int c = warp / kDecWpg, q = warp - c * kDecWpg;
+  int acc[2][2][4];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) acc[h][j][0] = acc[h][j][1] = acc[h][j][2] = acc[h][j][3] = 0;
+
+  if (warp == cwarps) {
+    // ---- TMA producer
+    if (lane == 0 && G > 0) {
+      const CUtensorMap* tm = G == cfg.gmax ? &tm_full : &tm_short;
+      prefetch_tensormap(tm);
+      prefetch_tensormap(&tm_act);
+      const uint32_t bytes = (uint32_t)G * 8 * kDecBoxK;
+      const int D = cfg.D;
+      const int early = min(nst, min(D, kDecEarlyStages));
+      for (int i = 0; i < early; ++i) {  // the ring is empty: no waits
+        mbar_arrive_expect_tx(&full[i], bytes);
+        tma_load_2d(stages + i * cfg.stage_bytes, tm, &full[i], k0 + i * kDecBoxK, n0);
+      }
+      if (p.pdl) pdl_wait();  // activations may come from the previous kernel
+      mbar_arrive_expect_tx(act_bar, (uint32_t)(nbox * cfg.arows * kDecABox));
+      for (int j = 0; j < nbox; ++j)
+        tma_load_2d(raw + j * (kDecRows * kDecABox), &tm_act, act_bar, (k0 + j * abox_k) * esz, 0);
+      for (int i = early; i < nst; ++i) {
+        const int s = i % D;
+        if (i >= D && !mbar_wait(&empty[s], ((i / D) & 1) ^ 1u, ERR_WAIT_EMPTY)) break;
+        mbar_arrive_expect_tx(&full[s], bytes);
+        tma_load_2d(stages + s * cfg.stage_bytes, tm, &full[s], k0 + i * kDecBoxK, n0);
+      }
+    }
+  } else {
+    const int g = lane >> 2;
+    const int sg = (g >> 1) + 4 * (g & 1);
+    const bool active = c < G;
+    const int col = n0 + 8 * c + sg;  // the weight column this lane transcodes
+    const bool col_ok = active && col < p.N;
+    const uint16_t sb = col_ok ? dec_scale_bits(p, col) : (uint16_t)0;
+    const int tid = threadIdx.x;
+    float scv = 0.0f, csv = 1.0f;
+    if (tid < 8 * G && n0 + tid < p.N) {
+      scv = __half2float(__ushort_as_half(dec_scale_bits(p, n0 + tid)));
+      if (p.col_scale_f32) csv = p.col_scale_f32[n0 + tid];
+    }
+    if (p.pdl) pdl_wait();  // per-row scales may come from the previous kernel
+    if (tid < 64) {
+      sc_s[tid] = scv;
+      cs_s[tid] = csv;
+    }
+    if (tid < kDecRows) {
+      const bool live = tid < p.M;
+      rg_s[tid] = live ? (p.row_g ? p.row_g[tid] : p.global_scale) : 0.0f;
+      rowinv_s[tid] = (live && p.row_inv_h) ? p.row_inv_h[tid] : p.a_inv_h;
+    }
+    const uint16_t inv = col_ok ? inv_scale_bits(sb) : (uint16_t)0x3C00u;
+    named_bar_sync(1, nthr);  // rowinv_s
+    DEC_TRACE(3);
+    if (nbox > 0) dec_wait(act_bar, 0, ERR_WAIT_FULL);
+    DEC_TRACE(9);
+    dec_quant_rows<AT>(raw, aq, cfg.astride, nbox, cfg.arows, rowinv_s, tid, nthr);
+    // CTA-uniform transcode choice; also the barrier that publishes the int8 rows
+    const bool all_fast = named_bar_and(2, nthr, fast_ok<FMT>(inv));
+    DEC_TRACE(4);
+    const uint32_t fs = fast_scale<FMT>(inv);
+    if (active) {
+      const uint32_t st_a = smem_u32(stages), aq_a = smem_u32(aq);
+      const bool hi_rows = p.M > 8;  // rows 8..15 of the m16 block hold data
+      if (all_fast)
+        dec_loop<FMT, true, kDecWpg>(acc, st_a, full, empty, aq_a, cfg.astride, cfg.stage_bytes, cfg.D, nst, c, q, lane,
+                            hi_rows, fs, inv);
+      else
+        dec_loop<FMT, false, kDecWpg>(acc, st_a, full, empty, aq_a, cfg.astride, cfg.stage_bytes, cfg.D, nst, c, q, lane,
+                             hi_rows, fs, inv);
+    }
+    DEC_TRACE(5);
+  }
+
+  // ---- reduction: the four accumulator sets, the two warps of a group,
+  // then (S = 2) the two CTAs
+  int a0 = (acc[0][0][0] + acc[0][1][0]) + (acc[1][0][0] + acc[1][1][0]);
+  int a1 = (acc[0][0][1] + acc[0][1][1]) + (acc[1][0][1] + acc[1][1][1]);
+  int a2 = (acc[0][0][2] + acc[0][1][2]) + (acc[1][0][2] + acc[1][1][2]);
+  int a3 = (acc[0][0][3] + acc[0][1][3]) + (acc[1][0][3] + acc[1][1][3]);
+  const int g = lane >> 2, t = lane & 3;
+  __syncthreads();
+  DEC_TRACE(6);
+  const bool frag = warp < cwarps && c < G;
+  // slot (c, 0) of tot receives group c's sums; the group's other warps park
+  // their fragments in slots (c, q) first
+  int32_t* fbase = tot + ((c * kDecWpg * kDecRows + g) * 8 + 2 * t);
+  int32_t* park = fbase + q * kDecRows * 8;
+  if (frag && q > 0) {
+    *reinterpret_cast<int2*>(park) = make_int2(a0, a1);
+    *reinterpret_cast<int2*>(park + 64) = make_int2(a2, a3);
+  }
+  __syncthreads();
+  if (frag && q == 0) {
+#pragma unroll
+    for (int w = 1; w < kDecWpg; ++w) {
+      const int32_t* pk = fbase + w * kDecRows * 8;
+      const int2 u = *reinterpret_cast<const int2*>(pk);
+      const int2 v = *reinterpret_cast<const int2*>(pk + 64);
+      a0 += u.x;
+      a1 += u.y;
+      a2 += v.x;
+      a3 += v.y;
+    }
+  }
+  if (S > 1) cluster_wait_acquire();  // the peer's barrier is initialised
+  if (frag && q == 0) {
+    if (c >= own_lo && c < own_hi) {
+      *reinterpret_cast<int2*>(fbase) = make_int2(a0, a1);
+      *reinterpret_cast<int2*>(fbase + 64) = make_int2(a2, a3);
+    } else {
+      const uint32_t peer = (uint32_t)(rank ^ 1);
+      const uint32_t rbar = map_to_rank(recv_bar, peer);
+      const int32_t* rb = recv + ((c * kDecRows + g) * 8 + 2 * t);
+      st_async_v2(map_to_rank(rb, peer), a0, a1, rbar);
+      st_async_v2(map_to_rank(rb + 64, peer), a2, a3, rbar);
+    }
+  }
+  __syncthreads();
+  if (S > 1) dec_wait(recv_bar, 0, ERR_WAIT_PEER);
+  DEC_TRACE(7);
+
+  // ---- epilogue of the owned groups
+  const int ncols = (own_hi - own_lo) * 8;
+  const int nel = ncols * p.M;
+  for (int e = threadIdx.x; e < nel; e += blockDim.x) {
+    int lc, m;
+    if (p.out_row_major) {
+      m = e / ncols;
+      lc = e - m * ncols;
+    } else {
+      lc = e / p.M;
+      m = e - lc * p.M;
+    }
+    const int cc = own_lo + (lc >> 3), j = lc & 7;
+    const int f = j < 4 ? 2 * j : 2 * (j - 4) + 1;  // MMA output column holding weight column j
+    const int n = n0 + 8 * cc + j;
+    if (n >= p.N) continue;
+    int32_t sum = tot[(cc * kDecWpg * kDecRows + m) * 8 + f];
+    if (S > 1) sum += recv[(cc * kDecRows + m) * 8 + f];
+    dec_store(p, n, m, sum, sc_s[8 * cc + j], cs_s[8 * cc + j], rg_s[m]);
+  }
+  DEC_TRACE(8);
+}
+
+std::atomic<int> g_decode_mode{1};
+
+template <int AT, int FMT>
+cudaError_t dec_launch(const GemvParams& p, const CUtensorMap& tf, const CUtensorMap& ts, const CUtensorMap& ta,
+                       const DecodeCfg& cfg, size_t smem, cudaStream_t stream) {
+  auto kern = decode_kernel<AT, FMT>;
+  cudaError_t e = ensure_smem_attr((const void*)kern, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(cfg.P * cfg.S, 1, 1);
+  lc.blockDim = dim3(cfg.gmax * kDecWpg * 32 + 32, 1, 1);
+  lc.dynamicSmemBytes = smem;
+  lc.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cfg.S;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = cfg.S > 1 ? 2 : 1;
+  return cudaLaunchKernelEx(&lc, kern, p, tf, ts, ta, cfg);
+}
+
+}  // namespace
+
+// Shape plan: S (1 or a CTA pair), groups per cluster, stage ring, shared
+// memory layout. Returns false when the shape does not fit one wave of at most
+// 8 groups per CTA with the CTA's whole activation slice in shared memory.
+static bool decode_plan(int M, int N, int K, int a_bytes, int sms, DecodeCfg* out, size_t* smem_out) {
+  if (M < 1 || M > kDecRows || N < 1 || K < 1) return false;
+  const int NG = (N + 7) / 8;
+  long long best = -1;
+  DecodeCfg cfg = {};
+  for (int S = 1; S <= 2; ++S) {
+    int P = sms / S;
+    if (P > NG) P = NG;
+    if (P < 1) continue;
+    const int gmax = (NG + P - 1) / P;
+    if (gmax > kDecMaxG) continue;
+    const int kper = ((K + S - 1) / S + kDecBoxK - 1) / kDecBoxK * kDecBoxK;
+    if (S > 1 && kper >= K) continue;  // nothing for the second CTA
+    const long long work = (long long)gmax * 8 * kper;
+    if (best < 0 || work < best) {
+      best = work;
+      cfg.S = S;
+      cfg.P = P;
+      cfg.NG = NG;
+      cfg.gmax = gmax;
+      cfg.kper = kper;
+    }
+  }
+  if (best < 0) return false;
+  const int nst = cfg.kper / kDecBoxK;
+  cfg.stage_bytes = cfg.gmax * 8 * kDecBoxK;
+  cfg.arows = M < kDecRows ? M : kDecRows;
+  cfg.astride = cfg.kper + 64;
+  const int abox_k = kDecABox / a_bytes;
+  const size_t raw = (size_t)((cfg.kper + abox_k - 1) / abox_k) * kDecRows * kDecABox;
+  const size_t fixed = (2 * kDecMaxStages + 2) * 8 + (64 + 64 + 16) * 4 + 16 * 2 + 64;
+  const size_t aqb = (size_t)kDecRows * cfg.astride;
+  const size_t red = (size_t)(kDecWpg + 1) * cfg.gmax * kDecRows * 8 * 4;
+  const size_t budget = 227 * 1024 - 1024;  // alignment slack
+  if (fixed + raw + aqb + red + (size_t)4 * cfg.stage_bytes > budget) return false;
+  int D = nst < kDecMaxStages ? nst : kDecMaxStages;
+  while (D > 4 && fixed + raw + aqb + red + (size_t)D * cfg.stage_bytes > budget) --D;
+  D -= D % kDecWpg;  // a multiple of the warps per group: warp q keeps ring slots s = q (mod kDecWpg)
+  if (D < kDecWpg) D = kDecWpg;
+  cfg.D = D;
+  size_t off = (size_t)D * cfg.stage_bytes;
+  cfg.off_raw = (int)off;  // 1024-aligned (stages are multiples of 1 KB)
+  off += raw;
+  cfg.off_aq = (int)off;
+  off += aqb;
+  off = (off + 15) & ~size_t(15);
+  cfg.off_tot = (int)off;
+  off += (size_t)cfg.gmax * kDecWpg * kDecRows * 8 * 4;
+  cfg.off_recv = (int)off;
+  off += (size_t)cfg.gmax * kDecRows * 8 * 4;
+  cfg.off_bar = (int)off;
+  off += (2 * kDecMaxStages + 2) * 8;
+  cfg.off_const = (int)off;
+  off += (64 + 64 + 16) * 4 + 16 * 2;
+  *out = cfg;
+  *smem_out = off + 1024;
+  return true;
+}
+
+bool decode_applicable(const GemvParams& p, int a_type, int fmt) {
+  if (g_decode_mode.load() == 0) return false;
+  if (fmt != 0 && fmt != 1) return false;  // int8-exact formats (E4M3 table, E5M2)
+  if (p.world > 1) return false;
+  DecodeCfg cfg;
+  size_t smem;
+  return decode_plan(p.M, p.N, p.K, a_type == A_S8 ? 1 : 2, num_sms_current(), &cfg, &smem);
+}
+
+cudaError_t launch_decode(const GemvParams& p, int a_type, int fmt, cudaStream_t stream) {
+  DecodeCfg cfg;
+  size_t smem = 0;
+  const int esz = a_type == A_S8 ? 1 : 2;
+  if (!decode_plan(p.M, p.N, p.K, esz, num_sms_current(), &cfg, &smem)) return cudaErrorInvalidValue;
+  CUtensorMap tf, ts, ta;
+  cudaError_t e = make_tmap_2d_u8(&tf, p.B, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)p.K, kDecBoxK,
+                                  (uint32_t)cfg.gmax * 8, /*swizzle128=*/true);
+  if (e != cudaSuccess) return e;
+  if (cfg.gmax > 1) {
+    e = make_tmap_2d_u8(&ts, p.B, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)p.K, kDecBoxK, (uint32_t)(cfg.gmax - 1) * 8,
+                        true);
+    if (e != cudaSuccess) return e;
+  } else {
+    ts = tf;
+  }
+  // activation rows as bytes: [M][K * esz], boxes of arows x 128 bytes
+  e = make_tmap_2d_u8(&ta, p.A, (uint64_t)p.K * esz, (uint64_t)p.M, (uint64_t)p.K * esz, kDecABox,
+                      (uint32_t)cfg.arows, false);
+  if (e != cudaSuccess) return e;
+  switch (a_type * 8 + fmt) {
+    case A_F16 * 8 + 0: return dec_launch<A_F16, FMT_E4M3_REF>(p, tf, ts, ta, cfg, smem, stream);
+    case A_F16 * 8 + 1: return dec_launch<A_F16, FMT_E5M2>(p, tf, ts, ta, cfg, smem, stream);
+    case A_BF16 * 8 + 0: return dec_launch<A_BF16, FMT_E4M3_REF>(p, tf, ts, ta, cfg, smem, stream);
+    case A_BF16 * 8 + 1: return dec_launch<A_BF16, FMT_E5M2>(p, tf, ts, ta, cfg, smem, stream);
+    case A_S8 * 8 + 0: return dec_launch<A_S8, FMT_E4M3_REF>(p, tf, ts, ta, cfg, smem, stream);
+    case A_S8 * 8 + 1: return dec_launch<A_S8, FMT_E5M2>(p, tf, ts, ta, cfg, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+void decode_set_mode(int mode) { g_decode_mode.store(mode); }
+unsigned int decode_device_error(bool clear) { return tu_device_error(clear); }
+cudaError_t decode_set_wait_limit(unsigned long long ns) { return tu_set_wait_limit(ns); }
+
+}  // namespace fp8imma_b200

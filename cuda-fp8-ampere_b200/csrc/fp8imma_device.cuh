@@ -132,14 +132,14 @@ __device__ __forceinline__ uint32_t transcode4_exact(uint32_t x, uint16_t inv_h)
 }
 
 // Whether a column may take the packed fast path below.
-//   E4M3: |inv| in [2^-6, 32]: inv/256 is then an exact fp16, and every
-//         subnormal input (true, or a killed NaN code) rounds to 0.
+//   E4M3: |inv| >= 2^-6 and finite: inv/256 is then an exact (normal) fp16,
+//         so (v*256)*(inv/256) is the exact product v*inv, rounded once.
 //   E5M2: inv finite and non-zero.
 template <int FMT>
 __device__ __forceinline__ bool fast_ok(uint16_t inv_h) {
   uint32_t a = inv_h & 0x7FFFu;
   if (FMT == FMT_E5M2) return a != 0u && a < 0x7C00u;
-  return a >= 0x2400u && a <= 0x5000u;
+  return a >= 0x2400u && a < 0x7C00u;
 }
 
 // Packed f16x2 constant for the fast path: inv/256 (E4M3) or inv (E5M2).
@@ -175,10 +175,21 @@ __device__ __forceinline__ uint32_t round_sat_pack(uint32_t p01, uint32_t p23) {
   return prmt(r01, r23, 0x6420u);
 }
 
+// 0xFF in every byte of t whose bit 7 is set, 0x00 elsewhere (byte permute
+// with sign replication)
+__device__ __forceinline__ uint32_t byte_sign_mask(uint32_t t) { return prmt(t, 0u, 0xBA98u); }
+
+// two E4M3FN bytes in each half of x -> f16x2 (bytes 0,1 -> lo; 2,3 -> hi)
+__device__ __forceinline__ void cvt_e4m3x4_f16x2x2(uint32_t x, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, l;\n\tcvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(x));
+}
+
 // Fast path, reference-E4M3 semantics, 4 bytes -> 4 int8.
-//   1. NaN codes (exponent 15, mantissa != 0) lose their exponent bits and
-//      become subnormal codes, which round to 0 below (the reference gives
-//      NaN -> 0).
+//   1. NaN codes (exponent 15, mantissa != 0) become code 0x00, which gives
+//      0 below (the reference gives NaN -> 0).
 //   2. Hardware E4M3FN decode is exact for exponent <= 14; the remaining
 //      exponent-15 codes (0x78 / 0xF8) decode to +-256.
 //   3. *256 is exact for |v| <= 240 and overflows +-256 to +-Inf (the
@@ -186,23 +197,21 @@ __device__ __forceinline__ uint32_t round_sat_pack(uint32_t p01, uint32_t p23) {
 //      same exact product v*inv as the reference, rounded once.
 //   4. round / saturate / pack.
 __device__ __forceinline__ uint32_t transcode4_fast_e4m3(uint32_t x, uint32_t inv256x2) {
-  uint32_t t = (x & 0x7F7F7F7Fu) + 0x07070707u;      // bit 7 set iff (b & 0x7F) >= 0x79
-  uint32_t kill = (t >> 4) & 0x08080808u;
-  x -= kill * 15u;                                  // clear bits 3..6 of killed bytes
-  uint32_t h01 = cvt_e4m3x2_f16x2(x & 0xFFFFu);
-  uint32_t h23 = cvt_e4m3x2_f16x2(x >> 16);
+  const uint32_t t = (x & 0x7F7F7F7Fu) + 0x07070707u;  // bit 7 set iff (b & 0x7F) >= 0x79
+  x &= ~byte_sign_mask(t);
+  uint32_t h01, h23;
+  cvt_e4m3x4_f16x2x2(x, h01, h23);
   const uint32_t k256 = 0x5C005C00u;
   h01 = hmul2_rn(hmul2_rn(h01, k256), inv256x2);
   h23 = hmul2_rn(hmul2_rn(h23, k256), inv256x2);
   return round_sat_pack(h01, h23);
 }
 
-// Fast path, E5M2 (fp16 = byte << 8): NaN codes (0x7D..0x7F) become
-// subnormal, Inf codes stay Inf.
+// Fast path, E5M2 (fp16 = byte << 8): NaN codes (0x7D..0x7F) become 0x00,
+// Inf codes stay Inf.
 __device__ __forceinline__ uint32_t transcode4_fast_e5m2(uint32_t x, uint32_t invx2) {
-  uint32_t t = (x & 0x7F7F7F7Fu) + 0x03030303u;      // bit 7 set iff (b & 0x7F) >= 0x7D
-  uint32_t kill = (t >> 5) & 0x04040404u;
-  x -= kill * 31u;                                  // clear bits 2..6
+  const uint32_t t = (x & 0x7F7F7F7Fu) + 0x03030303u;  // bit 7 set iff (b & 0x7F) >= 0x7D
+  x &= ~byte_sign_mask(t);
   uint32_t h01 = prmt(x, 0u, 0x1404u);
   uint32_t h23 = prmt(x, 0u, 0x3424u);
   h01 = hmul2_rn(h01, invx2);

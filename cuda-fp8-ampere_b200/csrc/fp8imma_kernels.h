@@ -43,6 +43,7 @@ struct GemvParams {
   unsigned long long peer_rows[8];          // this rank's output slice inside each rank's full output
   unsigned long long peer_sig[8];           // each rank's signal pad (u32 counters, epoch at kPeerEpochSlot)
   unsigned long long* trace;        // FP8IMMA_TRACE builds only: per-CTA phase timestamps
+  int dbg;                          // FP8IMMA_TRACE builds only: decode kernel experiment switches
 };
 
 // Signal pad layout (u32 words): [0, 8) arrival counters of the separate
@@ -58,17 +59,32 @@ cudaError_t ensure_smem_attr(const void* kernel, int bytes);
 cudaError_t make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
                             uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 
-// Device error words of the kernel files that wait on barriers (0 = none).
+// Device error words of the kernel files that wait on barriers (0 = none),
+// and their wait limits (current device).
 unsigned int gemv_device_error(bool clear);
+unsigned int decode_device_error(bool clear);
+cudaError_t gemv_set_wait_limit(unsigned long long ns);
+cudaError_t decode_set_wait_limit(unsigned long long ns);
+cudaError_t tc_set_wait_limit(unsigned long long ns);
+cudaError_t peer_set_wait_limit(unsigned long long ns);
 int num_sms_current();
 
 // Small-M split-K kernel (requires K % 16 == 0, 16-byte aligned A/B rows).
 // splits = 0 picks the K split from the shape.
 cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaStream_t stream);
+// whether the last launch_gemv_s8 on this thread ran the balanced decode kernel
+bool gemv_last_used_decode();
 int gemv_pick_splits(int N, int K, int mchunks, int num_sms);
 // Small-M kernel form: 1 (default) = stream-K where the cluster form would
 // need more than one wave, else clusters; 2 = always stream-K; 0 = never.
 void gemv_set_stream_k(int mode);
+
+// Balanced decode kernel (one CTA per SM, CTA pairs split K): int8-exact
+// formats, M <= 16, shapes that fit one wave of at most 8 column groups of 8
+// per CTA. decode_set_mode(0) turns it off (the split-K kernels run instead).
+bool decode_applicable(const GemvParams& p, int a_type, int fmt);
+cudaError_t launch_decode(const GemvParams& p, int a_type, int fmt, cudaStream_t stream);
+void decode_set_mode(int mode);
 
 // Large-M tensor-core path (tcgen05). Scratch must hold
 // gemm_tc_scratch_bytes() bytes (16-byte aligned).

@@ -962,15 +962,8 @@ cudaError_t launch_tc(const TcParams& p, const CUtensorMap& mw, const CUtensorMa
 
 void tc_set_pair_mode(bool on) { g_use_pair = on; }
 
-unsigned int tc_device_error(bool clear) {
-  unsigned int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_fp8imma_device_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
-  if (clear && v) {
-    unsigned int z = 0;
-    cudaMemcpyToSymbol(g_fp8imma_device_error, &z, sizeof(z));
-  }
-  return v;
-}
+unsigned int tc_device_error(bool clear) { return tu_device_error(clear); }
+cudaError_t tc_set_wait_limit(unsigned long long ns) { return tu_set_wait_limit(ns); }
 
 void tc_set_splitk(int splits) { g_tc_splitk = splits; }
 void tc_set_tile_x(int rows) { g_tc_tile_x = rows; }

@@ -51,8 +51,19 @@
       (p).trace[(size_t)cta_ * 16 + (i)] = t_;                                                             \
     }                                                                                                      \
   } while (0)
+// slot 15 holds the SM the CTA ran on
+#define TRACE_SMID(p)                                                                                      \
+  do {                                                                                                     \
+    if ((p).trace && threadIdx.x == 0) {                                                                   \
+      unsigned int s_;                                                                                     \
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(s_));                                                     \
+      const int cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);                    \
+      (p).trace[(size_t)cta_ * 16 + 15] = s_;                                                              \
+    }                                                                                                      \
+  } while (0)
 #else
 #define TRACE_POINT(p, i) do { } while (0)
+#define TRACE_SMID(p) do { } while (0)
 #endif
 
 namespace cg = cooperative_groups;
@@ -430,7 +441,7 @@ __device__ __forceinline__ void peer_signal_and_wait(const GemvParams& p, unsign
       unsigned int v;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
       if ((int)(v - target) >= 0) break;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > g_fp8imma_wait_limit_ns) {
         atomicCAS(&g_fp8imma_device_error, 0u, ERR_WAIT_PEER);
         break;
       }
@@ -461,6 +472,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int astride = FMT == FMT_WGT ? 2 * p.kc + 16 : p.kc + 64;
 
   if (threadIdx.x == 0) TRACE_POINT(p, 0);
+  TRACE_SMID(p);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -1019,7 +1031,13 @@ int gemv_pick_splits(int N, int K, int mchunks, int num_sms) {
 
 static cudaError_t launch_gemv_impl(GemvParams p, int a_type, int fmt, int splits, cudaStream_t stream);
 
+thread_local bool t_used_decode = false;
+bool gemv_last_used_decode() { return t_used_decode; }
+
 cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaStream_t stream) {
+  // shapes that fit one balanced wave (decode sizes) take the one-CTA-per-SM kernel
+  t_used_decode = splits == 0 && g_stream_k.load() != 2 && decode_applicable(p, a_type, fmt);
+  if (t_used_decode) return launch_decode(p, a_type, fmt, stream);
   // Every column tile stages and quantises its own copy of the activations;
   // when that repeated work is large (many tiles, M >= 16) the activations are
   // quantised once by a pre-pass and the kernel copies int8 rows instead.
@@ -1104,14 +1122,7 @@ static cudaError_t launch_gemv_impl(GemvParams p, int a_type, int fmt, int split
 
 void gemv_set_stream_k(int mode) { g_stream_k.store(mode); }
 
-unsigned int gemv_device_error(bool clear) {
-  unsigned int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_fp8imma_device_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
-  if (clear && v) {
-    unsigned int z = 0;
-    cudaMemcpyToSymbol(g_fp8imma_device_error, &z, sizeof(z));
-  }
-  return v;
-}
+unsigned int gemv_device_error(bool clear) { return tu_device_error(clear); }
+cudaError_t gemv_set_wait_limit(unsigned long long ns) { return tu_set_wait_limit(ns); }
 
 }  // namespace fp8imma_b200

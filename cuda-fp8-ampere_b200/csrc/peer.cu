@@ -20,7 +20,7 @@ namespace {
 
 static __device__ unsigned int g_peer_error;
 bool g_fused_gather = false;  // gather in the GEMM epilogue (else, default, a separate gather kernel)
-constexpr unsigned long long kPeerWaitNs = 2000000000ull;
+static __device__ unsigned long long g_peer_wait_ns = 2000000000ull;  // fp8imma_set_wait_limit_ns
 constexpr int kEpochSlot = kPeerEpochSlot;  // per-rank call counter (device-side epoch) in each rank's own pad
 constexpr int kGatherBlocks = 32;
 constexpr int kGatherThreads = 256;
@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(kGatherThreads) peer_gather_kernel(const __gri
       if ((int)(v - target) >= 0) break;
       unsigned long long now;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-      if (now - t0 > kPeerWaitNs) {
+      if (now - t0 > g_peer_wait_ns) {
         atomicCAS(&g_peer_error, 0u, 5u);
         break;
       }
@@ -113,6 +113,8 @@ cudaError_t launch_peer_gather(const unsigned long long* outs, const unsigned lo
                                                                    epoch);
   return cudaGetLastError();
 }
+
+cudaError_t peer_set_wait_limit(unsigned long long ns) { return cudaMemcpyToSymbol(g_peer_wait_ns, &ns, sizeof(ns)); }
 
 unsigned int peer_device_error(bool clear) {
   unsigned int v = 0;

@@ -7,6 +7,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_runtime.h>
 #include <cstdint>
 
 namespace fp8imma_dev {
@@ -24,6 +25,11 @@ enum : unsigned int {
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any healthy wait
+
+// The limit the waits use; kWaitLimitNs unless the host changed it
+// (fp8imma_set_wait_limit_ns). One per translation unit and device, like the
+// error word.
+static __device__ unsigned long long g_fp8imma_wait_limit_ns = kWaitLimitNs;
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
@@ -87,14 +93,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete: gives up
-// after kWaitLimitNs of wall time, records err_code and returns false.
+// after the wait limit (2 s unless changed) of wall time, records err_code and returns false.
 template <bool kSuspend = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int err_code) {
   if (mbar_try_wait<kSuspend>(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
+  const unsigned long long limit = *(volatile unsigned long long*)&g_fp8imma_wait_limit_ns;
   for (unsigned int i = 1;; ++i) {
     if (mbar_try_wait<kSuspend>(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    if (globaltimer_ns() - t0 > limit) break;
   }
   atomicCAS(&g_fp8imma_device_error, 0u, err_code);
   return false;
@@ -134,6 +141,21 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // named barrier among `count` threads (ids 1..15; 0 is __syncthreads)
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Host side, per translation unit (internal linkage: each kernel file reads
+// and sets its own copies of the device words on the current device).
+static inline unsigned int tu_device_error(bool clear) {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_fp8imma_device_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+  if (clear && v) {
+    unsigned int z = 0;
+    cudaMemcpyToSymbol(g_fp8imma_device_error, &z, sizeof(z));
+  }
+  return v;
+}
+static inline cudaError_t tu_set_wait_limit(unsigned long long ns) {
+  return cudaMemcpyToSymbol(g_fp8imma_wait_limit_ns, &ns, sizeof(ns));
 }
 
 }  // namespace fp8imma_dev

@@ -48,6 +48,8 @@ EXT_SYMBOLS = [
     "fp8imma_set_small_m_max",
     "fp8imma_last_path",
     "fp8imma_set_pdl",
+    "fp8imma_set_decode_kernel",
+    "fp8imma_set_wait_limit_ns",
     "fp8imma_set_tc_pair",
     "fp8imma_set_tc_splitk",
     "fp8imma_set_tc_tile_x",
@@ -121,6 +123,10 @@ def lib() -> ctypes.CDLL:
     L.fp8imma_set_tc_half_tail.argtypes = [I]
     L.fp8imma_set_pdl.restype = I
     L.fp8imma_set_pdl.argtypes = [I]
+    L.fp8imma_set_decode_kernel.restype = I
+    L.fp8imma_set_decode_kernel.argtypes = [I]
+    L.fp8imma_set_wait_limit_ns.restype = I
+    L.fp8imma_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]
     L.fp8imma_device_error.restype = ctypes.c_uint
     L.fp8imma_device_error.argtypes = [I]
     L.fp8imma_last_path.restype = I

@@ -174,21 +174,32 @@ int fp8imma_set_tc_tile_x(int rows);
 // than half of the CTA pairs idle, those tiles run as two half-width items
 // each (4096 x 4096: 34 of 256 tiles); 0: all tiles at full width.
 int fp8imma_set_tc_half_tail(int enable);
-// Programmatic dependent launch (default off). When on, a GEMM may start
+// 1 (default): small-M shapes that fit one wave of at most 64 weight columns
+// per SM (e.g. N = K = 4096) run the balanced decode kernel (one CTA per SM,
+// CTA pairs splitting K); 0: they run the split-K cluster kernel. Results are
+// identical either way. No reference counterpart (tuning switch).
+int fp8imma_set_decode_kernel(int enable);
+// Programmatic dependent launch (default on). A small-M GEMM then starts
 // streaming its weights and reading its column scales while the previous
 // kernel in the stream is still running; activations are read, and outputs
-// written, only after that kernel has finished. Enable it only when weights
-// and scales are not written by the kernel launched just before the GEMM.
+// written, only after that kernel has finished (a kernel launched after the
+// GEMM without the attribute is ordered as usual). Turn it off when weights or
+// scales are written by the kernel launched just before the GEMM.
 int fp8imma_set_pdl(int enable);
 // Kernel family the last fp8imma call on this thread launched:
 // 0 none, 1 small-M split-K, 2 generic fallback, 3 tcgen05 GEMM, 4 native FP8
-// tcgen05 GEMM, 5 native FP8 small-M split-K.
+// tcgen05 GEMM, 5 native FP8 small-M split-K, 6 balanced decode kernel.
 int fp8imma_last_path(void);
 const char* fp8imma_version(void);
 // Error word of the current device: non-zero when a kernel gave up a bounded
 // wait on its internal pipeline (the kernel then returned early and its output
 // is not valid). Synchronises the device. clear != 0 resets it.
 unsigned int fp8imma_device_error(int clear);
+// Wall-time limit of every bounded wait in the kernels (mbarrier pipelines,
+// the NVLink gather's peer flags) on the current device, in nanoseconds;
+// default 2e9. A wait that runs out records a code in the error word above and
+// lets its kernel finish. No reference counterpart (failure handling).
+int fp8imma_set_wait_limit_ns(unsigned long long ns);
 
 #ifdef __cplusplus
 }  // extern "C"

@@ -31,7 +31,9 @@ SHAPES = [(1, 128, 64), (3, 200, 528), (16, 4096, 4096), (37, 300, 1040), (64, 1
 def sk_mode(request, cuda):
     L = F.lib()
     assert L.fp8imma_set_stream_k(request.param) == 0
+    L.fp8imma_set_decode_kernel(0)  # these forms, not the balanced decode kernel
     yield request.param
+    L.fp8imma_set_decode_kernel(1)
     L.fp8imma_set_stream_k(1)
 
 

@@ -15,7 +15,8 @@ from helpers import cabi_ref_launch
 
 pytestmark = pytest.mark.gpu
 
-TC_PATH, GEMV_PATH, NATIVE_PATH, NATIVE_SK_PATH = 3, 1, 4, 5
+TC_PATH, NATIVE_PATH, NATIVE_SK_PATH = 3, 4, 5
+GEMV_PATHS = (1, 6)  # small-M split-K kernel, balanced decode kernel
 
 
 @pytest.fixture(params=[1, 0], ids=["pair", "single"])
@@ -37,7 +38,7 @@ def test_tc_reference_api_bitexact(tc_mode, variant, M, N, K):
     err, D = cabi_ref_launch(REF_FUNCS[variant], 32, dA, dB, ds, M, N, K, 0.37,
                              None if variant.startswith("v2") else 9.5)
     assert err == 0
-    assert L.fp8imma_last_path() == (TC_PATH if M > 64 else GEMV_PATH)
+    assert L.fp8imma_last_path() in ((TC_PATH,) if M > 64 else GEMV_PATHS)
     torch.cuda.synchronize()
     assert L.fp8imma_device_error(0) == 0
     eq = bits_equal(to_np_bits(D), D_o)
@@ -93,7 +94,7 @@ def test_tc_full_size_square4096_row_slices_and_splitk_agreement(tc_mode):
     try:
         D_sk, acc_sk = e.imma_fp8_gemm(inp.A, inp.B, inp.scales_u16, None, gs, ainv, "tensor", "e4m3", "int8",
                                        "float16", "col", True, None)
-        assert e.last_path() == GEMV_PATH
+        assert e.last_path() in GEMV_PATHS
     finally:
         L.fp8imma_set_small_m_max(64)
     torch.cuda.synchronize()
