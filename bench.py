@@ -6,7 +6,11 @@ with 1% outlier channels, through the reference-exact int8 path. One step =
 one GEMM call over one activation batch. With --gpus N (torchrun, one process
 per GPU) the layer is column-parallel: every rank owns a 4096-column shard of
 an N*4096-column weight (weak scaling), runs the same local GEMM and the
-shards are all-gathered over NCCL, which is part of the timed step.
+shards are gathered into every rank's full output, which is part of the
+timed step: by default over NVLink with this library's own peer stores and
+flags (fp8imma_gemm_allgather, --gather peer), or with the gather fused into
+the GEMM epilogue (--gather peer-epilogue) or an NCCL all-gather (--gather
+nccl).
 
 value       whole-job algorithmic GB/s (N*K + 4N + 2MK + 2MN bytes per GEMM),
             kernels on device-resident inputs, CUDA-graph replay, L2 defeated
@@ -261,14 +265,17 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    for i in range(args.warmup):
-        step(i)
+    # warm-up on the stream the graph is captured on (per-stream scratch such as
+    # the decode kernel's activation rows is set up outside the capture)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
     barrier()
     path_id = ext.last_path()
 
     # timed region: K steps captured in one CUDA graph (the NCCL all-gather of
     # the sharded layer included); eager launches if capture is refused
-    stream = torch.cuda.Stream()
     graph = None
     timing = "CUDA graph of K steps"
     try:
@@ -534,10 +541,11 @@ def time_points(ext, steps, only=None):
                 else:
                     ext.imma_fp8_gemm(A, Bs[i % copies], None, sig, 1.0, 1.0, "row", "e4m3", "fp8", "float16", "col",
                                       False, D)
-            for i in range(3):
-                call(i)
             g = torch.cuda.CUDAGraph()
             st = torch.cuda.Stream()
+            with torch.cuda.stream(st):  # per-stream scratch is set up before the capture
+                for i in range(3):
+                    call(i)
             torch.cuda.synchronize()
             with torch.cuda.graph(g, stream=st):
                 for i in range(n):

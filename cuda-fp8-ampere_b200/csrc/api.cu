@@ -33,6 +33,9 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 enum { FMT_E4M3_REF = 0, FMT_E5M2 = 1 };
 }  // namespace
 
+int api_pdl() { return g_pdl.load(); }
+int api_splitk() { return g_splitk.load(); }
+
 cudaError_t ensure_smem_attr(const void* kernel, int bytes) {
   if (bytes <= 48 * 1024) return cudaSuccess;
   static std::mutex mu;

@@ -55,7 +55,8 @@ constexpr int kDecMaxStages = 16;
 constexpr int kDecMaxThreads = kDecMaxG * kDecWpg * 32 + 32;
 constexpr int kDecEarlyStages = 4;  // weight stages requested before the activations
 constexpr int kDecRows = 16;        // activation rows (one m16 block)
-constexpr int kDecABox = 128;       // activation bytes per row per TMA box
+constexpr int kDecABox = 128;       // fp16/bf16 activation bytes per row per TMA box
+constexpr int kDecQBox = 64;        // int8 activation bytes per row per TMA box (direct layout)
 
 struct DecodeCfg {
   int S;            // CTAs per cluster (K split)
@@ -73,12 +74,16 @@ struct DecodeCfg {
 #ifdef FP8IMMA_TRACE
 // per CTA 64 words: [0] %globaltimer at entry, [1] SM id, [2, 16) clock64
 // cycles since entry at point i
-#define DEC_TRACE(i)                                                                                  \
-  do {                                                                                                \
-    if (p.trace && threadIdx.x == 0) p.trace[(size_t)blockIdx.x * 64 + (i)] = clock64() - trace_clk0; \
+// (kept in thread 0's registers and written at the end: a global store before
+// the barrier-initialisation fence would make the fence wait for it)
+#define DEC_TRACE(i)                                      \
+  do {                                                    \
+    if (threadIdx.x == 0) trace_pt[i] = clock64() - trace_clk0; \
   } while (0)
+#define DEC_DBG(bit) ((dbg & (bit)) != 0)
 #else
 #define DEC_TRACE(i) do { } while (0)
+#define DEC_DBG(bit) false
 #endif
 
 __device__ __forceinline__ void dec_mma(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -101,8 +106,8 @@ __device__ __forceinline__ uint16_t dec_scale_bits(const GemvParams& p, int n) {
   return p.scale_u16[n];
 }
 
-__device__ __forceinline__ void cluster_arrive_release() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait_acquire() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -150,32 +155,47 @@ __device__ __forceinline__ void dec_quant_rows(const uint8_t* raw, int8_t* aq, i
                                                const uint16_t* rowinv_s, int tid, int nthr) {
   const int per_box = arows * 8;
   const int total = nbox * per_box;
-  // item it = jb * per_box + rem, advanced without divisions
+  // item it = jb * per_box + rem, advanced without divisions; four items'
+  // shared loads in flight before any is converted
   const int djb = nthr / per_box, drem = nthr - djb * per_box;
   int jb = tid / per_box, rem = tid - jb * per_box;
-  for (int it = tid; it < total; it += nthr) {
-    const int r = rem >> 3, c = rem & 7;
-    const uint4 v = *reinterpret_cast<const uint4*>(raw + (size_t)jb * (kDecRows * kDecABox) + rem * 16);
-    if (AT == A_S8) {
-      *reinterpret_cast<uint4*>(aq + r * astride + jb * kDecABox + c * 16) = v;
-    } else {
-      const uint16_t ainv = rowinv_s[r];
-      const uint32_t ainv2 = (uint32_t)ainv | ((uint32_t)ainv << 16);
-      uint4 w = v;
-      if (AT == A_BF16) {
-        w.x = bf16x2_to_f16x2(w.x);
-        w.y = bf16x2_to_f16x2(w.y);
-        w.z = bf16x2_to_f16x2(w.z);
-        w.w = bf16x2_to_f16x2(w.w);
+  constexpr int kB = 4;
+  for (int base = tid; base < total; base += kB * nthr) {
+    uint4 v[kB];
+    int off[kB];
+    uint16_t ainv[kB];
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      const int r = rem >> 3, c = rem & 7;
+      off[j] = -1;
+      if (base + j * nthr < total) {
+        v[j] = *reinterpret_cast<const uint4*>(raw + (size_t)jb * (kDecRows * kDecABox) + rem * 16);
+        off[j] = r * astride + (AT == A_S8 ? jb * kDecABox + c * 16 : jb * (kDecABox / 2) + c * 8);
+        ainv[j] = rowinv_s[r];
       }
-      *reinterpret_cast<uint2*>(aq + r * astride + jb * (kDecABox / 2) + c * 8) =
-          make_uint2(quant4_f16(w.x, w.y, ainv2), quant4_f16(w.z, w.w, ainv2));
+      jb += djb;
+      rem += drem;
+      if (rem >= per_box) {
+        rem -= per_box;
+        ++jb;
+      }
     }
-    jb += djb;
-    rem += drem;
-    if (rem >= per_box) {
-      rem -= per_box;
-      ++jb;
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      if (off[j] < 0) break;
+      if (AT == A_S8) {
+        *reinterpret_cast<uint4*>(aq + off[j]) = v[j];
+      } else {
+        const uint32_t ainv2 = (uint32_t)ainv[j] | ((uint32_t)ainv[j] << 16);
+        uint4 w = v[j];
+        if (AT == A_BF16) {
+          w.x = bf16x2_to_f16x2(w.x);
+          w.y = bf16x2_to_f16x2(w.y);
+          w.z = bf16x2_to_f16x2(w.z);
+          w.w = bf16x2_to_f16x2(w.w);
+        }
+        *reinterpret_cast<uint2*>(aq + off[j]) = make_uint2(quant4_f16(w.x, w.y, ainv2), quant4_f16(w.z, w.w, ainv2));
+      }
     }
   }
 }
@@ -198,12 +218,18 @@ __device__ __forceinline__ void dec_store(const GemvParams& p, int n, int m, int
 
 // One stage of a consumer warp: this lane's 2 x 16 weight bytes, eight
 // transcodes, four MMAs into four accumulator sets.
+// Activation fragment layout: `a_half` bytes from K half 0 to half 1 of a
+// stage, `a_hi` bytes from rows 0..7 to rows 8..15.
 template <int FMT, bool FAST>
-__device__ __forceinline__ void dec_stage(int (&acc)[2][2][4], uint32_t w_addr, uint32_t a_addr, int astride,
-                                          bool hi_rows, uint32_t fs, uint16_t inv, int sw0, int sw1) {
+__device__ __forceinline__ void dec_stage(int (&acc)[2][2][4], uint32_t w_addr, uint32_t a_addr, int a_half, int a_hi,
+                                          bool hi_rows, uint32_t fs, uint16_t inv, int sw0, int sw1, int dbg) {
   const uint4 w0 = dec_lds128(w_addr + sw0);
   const uint4 w1 = dec_lds128(w_addr + sw1);
   uint32_t b[2][4];
+  if (DEC_DBG(4)) {  // experiment: no transcode
+    b[0][0] = w0.x; b[0][1] = w0.y; b[0][2] = w0.z; b[0][3] = w0.w;
+    b[1][0] = w1.x; b[1][1] = w1.y; b[1][2] = w1.z; b[1][3] = w1.w;
+  } else {
   b[0][0] = dec_tc4<FMT, FAST>(w0.x, fs, inv);
   b[0][1] = dec_tc4<FMT, FAST>(w0.y, fs, inv);
   b[0][2] = dec_tc4<FMT, FAST>(w0.z, fs, inv);
@@ -212,40 +238,135 @@ __device__ __forceinline__ void dec_stage(int (&acc)[2][2][4], uint32_t w_addr, 
   b[1][1] = dec_tc4<FMT, FAST>(w1.y, fs, inv);
   b[1][2] = dec_tc4<FMT, FAST>(w1.z, fs, inv);
   b[1][3] = dec_tc4<FMT, FAST>(w1.w, fs, inv);
+  }
+  if (DEC_DBG(2)) {  // experiment: no MMA
+    acc[0][0][0] ^= b[0][0] ^ b[0][1] ^ b[0][2] ^ b[0][3] ^ b[1][0] ^ b[1][1] ^ b[1][2] ^ b[1][3];
+    return;
+  }
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    const uint4 x = dec_lds128(a_addr + 64 * h);
+    const uint4 x = dec_lds128(a_addr + a_half * h);
     uint4 y = make_uint4(0u, 0u, 0u, 0u);
-    if (hi_rows) y = dec_lds128(a_addr + 8 * astride + 64 * h);
+    if (hi_rows) y = dec_lds128(a_addr + a_hi + a_half * h);
     dec_mma(acc[h][0], x.x, y.x, x.y, y.y, b[h][0], b[h][1]);
     dec_mma(acc[h][1], x.z, y.z, x.w, y.w, b[h][2], b[h][3]);
   }
 }
 
+// Two stages of a consumer warp at once: sixteen independent transcodes in
+// flight (the warp count per SM is low, so the latency is hidden inside the
+// warp), their MMAs into a second set of accumulators.
+template <int FMT, bool FAST>
+__device__ __forceinline__ void dec_stage2(int (&accA)[2][2][4], int (&accB)[2][2][4], uint32_t wA, uint32_t wB,
+                                           uint32_t aA, uint32_t aB, int a_half, int a_hi, bool hi_rows, uint32_t fs,
+                                           uint16_t inv, int sw0, int sw1) {
+  const uint4 x0 = dec_lds128(wA + sw0), x1 = dec_lds128(wA + sw1);
+  const uint4 y0 = dec_lds128(wB + sw0), y1 = dec_lds128(wB + sw1);
+  uint32_t bA[2][4], bB[2][4];
+  bA[0][0] = dec_tc4<FMT, FAST>(x0.x, fs, inv);
+  bB[0][0] = dec_tc4<FMT, FAST>(y0.x, fs, inv);
+  bA[0][1] = dec_tc4<FMT, FAST>(x0.y, fs, inv);
+  bB[0][1] = dec_tc4<FMT, FAST>(y0.y, fs, inv);
+  bA[0][2] = dec_tc4<FMT, FAST>(x0.z, fs, inv);
+  bB[0][2] = dec_tc4<FMT, FAST>(y0.z, fs, inv);
+  bA[0][3] = dec_tc4<FMT, FAST>(x0.w, fs, inv);
+  bB[0][3] = dec_tc4<FMT, FAST>(y0.w, fs, inv);
+  bA[1][0] = dec_tc4<FMT, FAST>(x1.x, fs, inv);
+  bB[1][0] = dec_tc4<FMT, FAST>(y1.x, fs, inv);
+  bA[1][1] = dec_tc4<FMT, FAST>(x1.y, fs, inv);
+  bB[1][1] = dec_tc4<FMT, FAST>(y1.y, fs, inv);
+  bA[1][2] = dec_tc4<FMT, FAST>(x1.z, fs, inv);
+  bB[1][2] = dec_tc4<FMT, FAST>(y1.z, fs, inv);
+  bA[1][3] = dec_tc4<FMT, FAST>(x1.w, fs, inv);
+  bB[1][3] = dec_tc4<FMT, FAST>(y1.w, fs, inv);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint4 u = dec_lds128(aA + a_half * h);
+    const uint4 v = dec_lds128(aB + a_half * h);
+    uint4 u8 = make_uint4(0u, 0u, 0u, 0u), v8 = make_uint4(0u, 0u, 0u, 0u);
+    if (hi_rows) {
+      u8 = dec_lds128(aA + a_hi + a_half * h);
+      v8 = dec_lds128(aB + a_hi + a_half * h);
+    }
+    dec_mma(accA[h][0], u.x, u8.x, u.y, u8.y, bA[h][0], bA[h][1]);
+    dec_mma(accA[h][1], u.z, u8.z, u.w, u8.w, bA[h][2], bA[h][3]);
+    dec_mma(accB[h][0], v.x, v8.x, v.y, v8.y, bB[h][0], bB[h][1]);
+    dec_mma(accB[h][1], v.z, v8.z, v.w, v8.w, bB[h][2], bB[h][3]);
+  }
+}
+
+// Activation layouts: quantised in the kernel (direct = false: row stride
+// astride, K contiguous) or copied by TMA as int8 boxes of 16 rows x 64 bytes
+// (direct = true: box j = K bytes [64j, 64j + 64) at j * 1024, rows 64 bytes
+// apart, so each 8-lane phase of a fragment load covers all 32 banks).
 template <int FMT, bool FAST, int W>
 __device__ __forceinline__ bool dec_loop(int (&acc)[2][2][4], uint32_t stages_a, uint64_t* full, uint64_t* empty,
-                                         uint32_t aq_a, int astride, int stage_bytes, int D, int nst, int c, int q,
-                                         int lane, bool hi_rows, uint32_t fs, uint16_t inv) {
+                                         uint32_t aq_a, bool direct, int astride, int stage_bytes, int D, int nst,
+                                         int c, int q, int lane, bool hi_rows, uint32_t fs, uint16_t inv, int dbg) {
   const int g = lane >> 2, t = lane & 3;
   const int sg = (g >> 1) + 4 * (g & 1);
   const uint32_t wrow = stages_a + (8 * c + sg) * kDecBoxK;
   const int sw0 = (t ^ sg) << 4, sw1 = ((4 + t) ^ sg) << 4;  // 16-byte chunks of halves 0 and 1 (swizzled)
-  uint32_t a_addr = aq_a + g * astride + 16 * t + q * kDecBoxK;
+  const int a_half = direct ? kDecRows * kDecQBox : 64;
+  const int a_hi = direct ? 8 * kDecQBox : 8 * astride;
+  const int a_stage = direct ? 2 * kDecRows * kDecQBox : kDecBoxK;  // bytes per 128-K stage
+  uint32_t a_addr = aq_a + (direct ? g * kDecQBox : g * astride) + 16 * t + q * a_stage;
   bool ok = true;
   int s = q;
   uint32_t phase = 0;
-  for (int i = q; i < nst; i += W) {
-    if (ok) ok = dec_wait(&full[s], phase, ERR_WAIT_FULL);
-    dec_stage<FMT, FAST>(acc, wrow + s * stage_bytes, a_addr, astride, hi_rows, fs, inv, sw0, sw1);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-    a_addr += W * kDecBoxK;
-    s += W;
-    if (s >= D) {
-      s -= D;
-      phase ^= 1u;
+  const bool recycle = nst > D;
+  int acc2[2][2][4];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) acc2[h][j][0] = acc2[h][j][1] = acc2[h][j][2] = acc2[h][j][3] = 0;
+  auto advance = [&](int& slot, uint32_t& ph) {
+    slot += W;
+    if (slot >= D) {
+      slot -= D;
+      ph ^= 1u;
     }
+  };
+  int i = q;
+  // two stages at a time, except when the ring recycles with fewer than 2W
+  // slots: the second stage's slot could then still wait for the first's release
+  const int pair_end = (recycle && D < 2 * W) ? q : nst;
+  for (; i + W < pair_end; i += 2 * W) {
+    int s2 = s;
+    uint32_t phase2 = phase;
+    advance(s2, phase2);
+    if (ok && !DEC_DBG(1)) ok = dec_wait(&full[s], phase, ERR_WAIT_FULL);
+    if (ok && !DEC_DBG(1)) ok = dec_wait(&full[s2], phase2, ERR_WAIT_FULL);
+    dec_stage2<FMT, FAST>(acc, acc2, wrow + s * stage_bytes, wrow + s2 * stage_bytes, a_addr, a_addr + W * a_stage,
+                          a_half, a_hi, hi_rows, fs, inv, sw0, sw1);
+    if (recycle) {  // the producer refills these slots: release them once every lane has read them
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&empty[s]);
+        mbar_arrive(&empty[s2]);
+      }
+    }
+    a_addr += 2 * W * a_stage;
+    s = s2;
+    phase = phase2;
+    advance(s, phase);
   }
+  for (; i < nst; i += W) {
+    if (ok && !DEC_DBG(1)) ok = dec_wait(&full[s], phase, ERR_WAIT_FULL);
+    dec_stage<FMT, FAST>(acc, wrow + s * stage_bytes, a_addr, a_half, a_hi, hi_rows, fs, inv, sw0, sw1, dbg);
+    if (recycle) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    a_addr += W * a_stage;
+    advance(s, phase);
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int x = 0; x < 4; ++x) acc[h][j][x] += acc2[h][j][x];
   return ok;
 }
 
@@ -258,12 +379,8 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 #ifdef FP8IMMA_TRACE
   const long long trace_clk0 = clock64();
-  if (p.trace && threadIdx.x == 0) {
-    unsigned int sm_;
-    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm_));
-    p.trace[(size_t)blockIdx.x * 64 + 0] = globaltimer_ns();
-    p.trace[(size_t)blockIdx.x * 64 + 1] = sm_;
-  }
+  const unsigned long long trace_gt0 = globaltimer_ns();
+  long long trace_pt[16] = {0};
 #endif
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + cfg.off_bar);
@@ -285,19 +402,33 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
   const int S = cfg.S;
   const int rank = S > 1 ? (int)cluster_ctarank() : 0;
   const int pc = blockIdx.x / S;
-  const int cg0 = (int)((long long)pc * cfg.NG / cfg.P);
-  const int G = (int)((long long)(pc + 1) * cfg.NG / cfg.P) - cg0;
+  const int cg0 = pc * cfg.NG / cfg.P;  // (fits in 32 bits: pc < 148, NG < 2^24)
+  const int G = (pc + 1) * cfg.NG / cfg.P - cg0;
   const int n0 = cg0 * 8;
   const int k0 = rank * cfg.kper;
   const int k1 = min(p.K, k0 + cfg.kper);
   const int nst = k1 > k0 ? (k1 - k0 + kDecBoxK - 1) / kDecBoxK : 0;
+  constexpr bool kDirect = AT == A_S8;  // int8 rows: TMA straight into the fragment layout
   const int esz = AT == A_S8 ? 1 : 2;
-  const int abox_k = kDecABox / esz;  // activation K elements per box
+  const int abox_k = kDirect ? kDecQBox : kDecABox / esz;  // activation K elements per box
+  const int abox_bytes = kDirect ? kDecQBox : kDecABox;      // bytes per row per box
+  const int abox_slot = kDecRows * abox_bytes;                // shared memory per box
   const int nbox = k1 > k0 ? (k1 - k0 + abox_k - 1) / abox_k : 0;
   const int gh = (G + 1) >> 1;  // groups [0, gh) finish on rank 0, [gh, G) on rank 1
   const int own_lo = rank == 0 ? 0 : gh, own_hi = (S == 1 || rank == 1) ? G : gh;
 
-  if (threadIdx.x == 0) {
+  // The producer thread initialises the barriers and issues the first weight
+  // stages (and, without programmatic dependent launch, the activation rows)
+  // before the CTA-wide barrier: nothing waits on them before it.
+  const CUtensorMap* tm = G == cfg.gmax ? &tm_full : &tm_short;
+  const uint32_t wbytes = (uint32_t)G * 8 * kDecBoxK;
+  const int early = min(nst, min(cfg.D, kDecEarlyStages));
+  uint8_t* adst = kDirect ? reinterpret_cast<uint8_t*>(aq) : raw;
+  const bool producer = warp == cwarps && lane == 0 && G > 0;
+  DEC_TRACE(10);
+  if (producer) {
+    prefetch_tensormap(tm);
+    prefetch_tensormap(&tm_act);
     for (int s = 0; s < cfg.D; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], G);
@@ -305,10 +436,23 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
     mbar_init(recv_bar, 1);
     mbar_init(act_bar, 1);
     fence_barrier_init();
+    // a few weight stages (which, with programmatic dependent launch, stream
+    // while the previous kernel finishes), then the activation rows, then the
+    // rest (measured faster than the rows first: the one burst of every stage
+    // at once delayed the whole stream)
+    for (int i = 0; i < early; ++i) {  // the ring is empty: no waits
+      mbar_arrive_expect_tx(&full[i], wbytes);
+      tma_load_2d(stages + i * cfg.stage_bytes, tm, &full[i], k0 + i * kDecBoxK, n0);
+    }
+    if (!p.pdl) {
+      mbar_arrive_expect_tx(act_bar, (uint32_t)(nbox * cfg.arows * abox_bytes));
+      for (int j = 0; j < nbox; ++j) tma_load_2d(adst + j * abox_slot, &tm_act, act_bar, (k0 + j * abox_k) * esz, 0);
+    }
   }
+  DEC_TRACE(11);
   __syncthreads();
   if (S > 1) {
-    cluster_arrive_release();  // publishes the barrier initialisation to the peer
+    cluster_arrive_relaxed();  // the initialisation fence above publishes the barriers to the peer
     if (threadIdx.x == 0) mbar_arrive_expect_tx(recv_bar, (uint32_t)((own_hi - own_lo) * kDecRows * 8 * 4));
   }
   if (p.pdl) pdl_launch_dependents();  // the next grid may take SMs as this one's CTAs exit
@@ -322,26 +466,19 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
     for (int j = 0; j < 2; ++j) acc[h][j][0] = acc[h][j][1] = acc[h][j][2] = acc[h][j][3] = 0;
 
   if (warp == cwarps) {
-    // ---- TMA producer
-    if (lane == 0 && G > 0) {
-      const CUtensorMap* tm = G == cfg.gmax ? &tm_full : &tm_short;
-      prefetch_tensormap(tm);
-      prefetch_tensormap(&tm_act);
-      const uint32_t bytes = (uint32_t)G * 8 * kDecBoxK;
+    // ---- TMA producer: the activation rows (after the previous kernel when
+    // launched as a programmatic dependent), then the remaining weight stages
+    if (producer) {
       const int D = cfg.D;
-      const int early = min(nst, min(D, kDecEarlyStages));
-      for (int i = 0; i < early; ++i) {  // the ring is empty: no waits
-        mbar_arrive_expect_tx(&full[i], bytes);
-        tma_load_2d(stages + i * cfg.stage_bytes, tm, &full[i], k0 + i * kDecBoxK, n0);
+      if (p.pdl) {
+        pdl_wait();  // activations may come from the previous kernel
+        mbar_arrive_expect_tx(act_bar, (uint32_t)(nbox * cfg.arows * abox_bytes));
+        for (int j = 0; j < nbox; ++j) tma_load_2d(adst + j * abox_slot, &tm_act, act_bar, (k0 + j * abox_k) * esz, 0);
       }
-      if (p.pdl) pdl_wait();  // activations may come from the previous kernel
-      mbar_arrive_expect_tx(act_bar, (uint32_t)(nbox * cfg.arows * kDecABox));
-      for (int j = 0; j < nbox; ++j)
-        tma_load_2d(raw + j * (kDecRows * kDecABox), &tm_act, act_bar, (k0 + j * abox_k) * esz, 0);
       for (int i = early; i < nst; ++i) {
         const int s = i % D;
         if (i >= D && !mbar_wait(&empty[s], ((i / D) & 1) ^ 1u, ERR_WAIT_EMPTY)) break;
-        mbar_arrive_expect_tx(&full[s], bytes);
+        mbar_arrive_expect_tx(&full[s], wbytes);
         tma_load_2d(stages + s * cfg.stage_bytes, tm, &full[s], k0 + i * kDecBoxK, n0);
       }
     }
@@ -373,7 +510,7 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
     DEC_TRACE(3);
     if (nbox > 0) dec_wait(act_bar, 0, ERR_WAIT_FULL);
     DEC_TRACE(9);
-    dec_quant_rows<AT>(raw, aq, cfg.astride, nbox, cfg.arows, rowinv_s, tid, nthr);
+    if (!kDirect) dec_quant_rows<AT>(raw, aq, cfg.astride, nbox, cfg.arows, rowinv_s, tid, nthr);
     // CTA-uniform transcode choice; also the barrier that publishes the int8 rows
     const bool all_fast = named_bar_and(2, nthr, fast_ok<FMT>(inv));
     DEC_TRACE(4);
@@ -381,12 +518,17 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
     if (active) {
       const uint32_t st_a = smem_u32(stages), aq_a = smem_u32(aq);
       const bool hi_rows = p.M > 8;  // rows 8..15 of the m16 block hold data
+#ifdef FP8IMMA_TRACE
+      const int dbg = p.dbg;
+#else
+      const int dbg = 0;
+#endif
       if (all_fast)
-        dec_loop<FMT, true, kDecWpg>(acc, st_a, full, empty, aq_a, cfg.astride, cfg.stage_bytes, cfg.D, nst, c, q, lane,
-                            hi_rows, fs, inv);
+        dec_loop<FMT, true, kDecWpg>(acc, st_a, full, empty, aq_a, kDirect, cfg.astride, cfg.stage_bytes, cfg.D, nst,
+                                     c, q, lane, hi_rows, fs, inv, dbg);
       else
-        dec_loop<FMT, false, kDecWpg>(acc, st_a, full, empty, aq_a, cfg.astride, cfg.stage_bytes, cfg.D, nst, c, q, lane,
-                             hi_rows, fs, inv);
+        dec_loop<FMT, false, kDecWpg>(acc, st_a, full, empty, aq_a, kDirect, cfg.astride, cfg.stage_bytes, cfg.D, nst,
+                                      c, q, lane, hi_rows, fs, inv, dbg);
     }
     DEC_TRACE(5);
   }
@@ -442,15 +584,14 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
   // ---- epilogue of the owned groups
   const int ncols = (own_hi - own_lo) * 8;
   const int nel = ncols * p.M;
+  // e / d by multiply-high: exact for e < 2^28 and d <= 64
+  const int dv = p.out_row_major ? ncols : p.M;
+  const unsigned int magic = dv > 0 ? 0xFFFFFFFFu / (unsigned int)dv + 1u : 0u;
   for (int e = threadIdx.x; e < nel; e += blockDim.x) {
-    int lc, m;
-    if (p.out_row_major) {
-      m = e / ncols;
-      lc = e - m * ncols;
-    } else {
-      lc = e / p.M;
-      m = e - lc * p.M;
-    }
+    const int qt = dv == 1 ? e : (int)__umulhi((unsigned int)e, magic);
+    const int rm = e - qt * dv;
+    const int lc = p.out_row_major ? rm : qt;
+    const int m = p.out_row_major ? qt : rm;
     const int cc = own_lo + (lc >> 3), j = lc & 7;
     const int f = j < 4 ? 2 * j : 2 * (j - 4) + 1;  // MMA output column holding weight column j
     const int n = n0 + 8 * cc + j;
@@ -460,9 +601,48 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
     dec_store(p, n, m, sum, sc_s[8 * cc + j], cs_s[8 * cc + j], rg_s[m]);
   }
   DEC_TRACE(8);
+#ifdef FP8IMMA_TRACE
+  if (p.trace && threadIdx.x == 0) {
+    unsigned int sm_;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm_));
+    p.trace[(size_t)blockIdx.x * 64 + 0] = trace_gt0;
+    p.trace[(size_t)blockIdx.x * 64 + 1] = sm_;
+#pragma unroll
+    for (int i = 2; i < 16; ++i) p.trace[(size_t)blockIdx.x * 64 + i] = trace_pt[i];
+  }
+#endif
+}
+
+// Activation pre-pass: the rows quantised once, for every CTA of the decode
+// grid to copy (without it each CTA pair quantises all of A for its K half).
+// Launched as a programmatic dependent when PDL is on: its CTAs start next to
+// the previous kernel's and wait for it (griddepcontrol.wait) before reading
+// A or writing the rows that the previous call's kernel may still be reading.
+template <int AT>
+__global__ void __launch_bounds__(256) dec_quant_kernel(const void* __restrict__ A, int M, int K, uint16_t a_inv_h,
+                                                        const uint16_t* __restrict__ row_inv_h,
+                                                        int8_t* __restrict__ Aq) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int items = K >> 3;  // 8 values per item
+  const size_t total = (size_t)M * items;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / items);
+    uint4 v = reinterpret_cast<const uint4*>(A)[i];
+    const uint16_t ainv = row_inv_h ? row_inv_h[m] : a_inv_h;
+    const uint32_t ainv2 = (uint32_t)ainv | ((uint32_t)ainv << 16);
+    if (AT == A_BF16) {
+      v.x = bf16x2_to_f16x2(v.x);
+      v.y = bf16x2_to_f16x2(v.y);
+      v.z = bf16x2_to_f16x2(v.z);
+      v.w = bf16x2_to_f16x2(v.w);
+    }
+    reinterpret_cast<uint2*>(Aq)[i] = make_uint2(quant4_f16(v.x, v.y, ainv2), quant4_f16(v.z, v.w, ainv2));
+  }
 }
 
 std::atomic<int> g_decode_mode{1};
+constexpr int kDecPrepassM = 1;  // rows from which the pre-pass beats per-CTA quantisation
 
 template <int AT, int FMT>
 cudaError_t dec_launch(const GemvParams& p, const CUtensorMap& tf, const CUtensorMap& ts, const CUtensorMap& ta,
@@ -520,10 +700,13 @@ static bool decode_plan(int M, int N, int K, int a_bytes, int sms, DecodeCfg* ou
   cfg.stage_bytes = cfg.gmax * 8 * kDecBoxK;
   cfg.arows = M < kDecRows ? M : kDecRows;
   cfg.astride = cfg.kper + 64;
-  const int abox_k = kDecABox / a_bytes;
-  const size_t raw = (size_t)((cfg.kper + abox_k - 1) / abox_k) * kDecRows * kDecABox;
+  // int8 rows (a_bytes == 1) go straight into the fragment layout; 16-bit
+  // rows are staged raw and quantised into a row-strided int8 copy
+  const bool direct = a_bytes == 1;
+  const size_t raw = direct ? 0 : (size_t)((cfg.kper + 63) / 64) * kDecRows * kDecABox;
   const size_t fixed = (2 * kDecMaxStages + 2) * 8 + (64 + 64 + 16) * 4 + 16 * 2 + 64;
-  const size_t aqb = (size_t)kDecRows * cfg.astride;
+  const size_t aqb = direct ? (size_t)((cfg.kper + kDecQBox - 1) / kDecQBox) * kDecRows * kDecQBox
+                            : (size_t)kDecRows * cfg.astride;
   const size_t red = (size_t)(kDecWpg + 1) * cfg.gmax * kDecRows * 8 * 4;
   const size_t budget = 227 * 1024 - 1024;  // alignment slack
   if (fixed + raw + aqb + red + (size_t)4 * cfg.stage_bytes > budget) return false;
@@ -557,14 +740,43 @@ bool decode_applicable(const GemvParams& p, int a_type, int fmt) {
   if (p.world > 1) return false;
   DecodeCfg cfg;
   size_t smem;
-  return decode_plan(p.M, p.N, p.K, a_type == A_S8 ? 1 : 2, num_sms_current(), &cfg, &smem);
+  // rows quantised by the pre-pass arrive as int8 (half the shared memory)
+  const bool prepass = a_type != A_S8 && p.M >= kDecPrepassM && !p.no_alloc;
+  return decode_plan(p.M, p.N, p.K, (a_type == A_S8 || prepass) ? 1 : 2, num_sms_current(), &cfg, &smem);
 }
 
-cudaError_t launch_decode(const GemvParams& p, int a_type, int fmt, cudaStream_t stream) {
+cudaError_t launch_decode(const GemvParams& p_in, int a_type, int fmt, cudaStream_t stream) {
+  GemvParams p = p_in;
+  if (a_type != A_S8 && p.M >= kDecPrepassM && !p.no_alloc) {
+    void* aq = stream_scratch(stream, (size_t)p.M * p.K, 1);
+    if (aq) {
+      const size_t total = (size_t)p.M * (p.K >> 3);
+      cudaLaunchConfig_t lc = {};
+      lc.gridDim = dim3((unsigned)((total + 255) / 256), 1, 1);
+      lc.blockDim = dim3(256, 1, 1);
+      lc.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
+      lc.attrs = attr;
+      lc.numAttrs = 1;
+      cudaError_t e = a_type == A_BF16
+                          ? cudaLaunchKernelEx(&lc, dec_quant_kernel<A_BF16>, p.A, p.M, p.K, p.a_inv_h, p.row_inv_h,
+                                               static_cast<int8_t*>(aq))
+                          : cudaLaunchKernelEx(&lc, dec_quant_kernel<A_F16>, p.A, p.M, p.K, p.a_inv_h, p.row_inv_h,
+                                               static_cast<int8_t*>(aq));
+      if (e != cudaSuccess) return e;
+      p.A = aq;
+      p.row_inv_h = nullptr;
+      p.pdl = 1;  // weights stream while the pre-pass runs; the rows are read after it
+      a_type = A_S8;
+    }
+  }
   DecodeCfg cfg;
   size_t smem = 0;
   const int esz = a_type == A_S8 ? 1 : 2;
-  if (!decode_plan(p.M, p.N, p.K, esz, num_sms_current(), &cfg, &smem)) return cudaErrorInvalidValue;
+  // (only when the pre-pass could not get its scratch and 16-bit rows do not fit)
+  if (!decode_plan(p.M, p.N, p.K, esz, num_sms_current(), &cfg, &smem)) return cudaErrorNotSupported;
   CUtensorMap tf, ts, ta;
   cudaError_t e = make_tmap_2d_u8(&tf, p.B, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)p.K, kDecBoxK,
                                   (uint32_t)cfg.gmax * 8, /*swizzle128=*/true);
@@ -577,8 +789,9 @@ cudaError_t launch_decode(const GemvParams& p, int a_type, int fmt, cudaStream_t
     ts = tf;
   }
   // activation rows as bytes: [M][K * esz], boxes of arows x 128 bytes
-  e = make_tmap_2d_u8(&ta, p.A, (uint64_t)p.K * esz, (uint64_t)p.M, (uint64_t)p.K * esz, kDecABox,
-                      (uint32_t)cfg.arows, false);
+  // (16-bit rows) or arows x 64 bytes (int8 rows, the fragment layout)
+  e = make_tmap_2d_u8(&ta, p.A, (uint64_t)p.K * esz, (uint64_t)p.M, (uint64_t)p.K * esz,
+                      esz == 1 ? kDecQBox : kDecABox, (uint32_t)cfg.arows, false);
   if (e != cudaSuccess) return e;
   switch (a_type * 8 + fmt) {
     case A_F16 * 8 + 0: return dec_launch<A_F16, FMT_E4M3_REF>(p, tf, ts, ta, cfg, smem, stream);

@@ -55,6 +55,17 @@ constexpr int kPeerFusedEpochSlot = 33;
 
 cudaError_t ensure_smem_attr(const void* kernel, int bytes);
 
+// process-wide settings of the C ABI (fp8imma_set_pdl, fp8imma_set_splitk)
+int api_pdl();
+int api_splitk();
+
+// Scratch memory owned by (current device, stream, tag): allocated on first
+// use (zero-filled) and grown on demand, never freed; nullptr while the
+// stream is capturing a graph and no large enough buffer exists yet (callers
+// then take a path without scratch). *fresh tells whether the buffer was just
+// (re)allocated. Tags: 0 stream-K partials, 1 decode activation rows.
+void* stream_scratch(cudaStream_t stream, size_t bytes, int tag, bool* fresh = nullptr);
+
 // TMA descriptor for a 2-D byte tensor [outer][inner] (row pitch row_bytes).
 cudaError_t make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
                             uint32_t box_inner, uint32_t box_outer, bool swizzle128);

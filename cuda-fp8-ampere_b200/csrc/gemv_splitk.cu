@@ -414,13 +414,21 @@ __device__ __forceinline__ void peer_copy(const GemvParams& p, int n_lo, int n_h
 // After the cluster barrier that ends the kernel (which orders every CTA's
 // peer stores of the cluster before it): the cluster's first CTA publishes
 // them with one system-scope release per peer, and the grid's first CTA waits
-// until every peer has published all of its clusters for this call.
+// until every peer has published all of its clusters for this call. Every
+// call adds exactly kPeerCallUnits to each counter whatever its grid (cluster
+// i adds its share floor((i+1)U/n) - floor(iU/n) of U over n clusters), so
+// calls of different shapes in a row keep the per-call targets e * U aligned.
+constexpr unsigned int kPeerCallUnits = 1u << 20;
+
 __device__ __forceinline__ void peer_signal_and_wait(const GemvParams& p, unsigned int cluster_rank,
-                                                     unsigned int clusters, unsigned int* target_s) {
+                                                     unsigned int clusters, unsigned int cluster_id,
+                                                     unsigned int* target_s) {
   if (cluster_rank != 0) return;
   if ((int)threadIdx.x < p.world && (int)threadIdx.x != p.rank) {
+    const unsigned long long U = kPeerCallUnits;
+    const unsigned int share = (unsigned int)(((cluster_id + 1ull) * U) / clusters - ((unsigned long long)cluster_id * U) / clusters);
     unsigned int* slot = reinterpret_cast<unsigned int*>(p.peer_sig[threadIdx.x]) + kPeerFusedSlot + p.rank;
-    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(slot) : "memory");
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(slot), "r"(share) : "memory");
   }
   if (blockIdx.x != 0 || blockIdx.y != 0 || blockIdx.z != 0) return;
   if (threadIdx.x == 0) {
@@ -430,7 +438,7 @@ __device__ __forceinline__ void peer_signal_and_wait(const GemvParams& p, unsign
       e = *ctr + 1;
       *ctr = e;
     }
-    *target_s = e * clusters;
+    *target_s = e * kPeerCallUnits;  // modulo 2^32; compared by signed difference below
   }
   __syncthreads();
   const unsigned int target = *target_s;
@@ -640,6 +648,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (threadIdx.x == 0) TRACE_POINT(p, 8);
   if (p.world > 1)
     peer_signal_and_wait(p, (unsigned int)rank, (gridDim.x * gridDim.y * gridDim.z) / (unsigned int)S,
+                         blockIdx.x + gridDim.x * blockIdx.z,  // clusters span y (the K slices)
                          reinterpret_cast<unsigned int*>(smem + kBarOffset + 128));
 }
 
@@ -974,47 +983,21 @@ cudaError_t launch_mb(const GemvParams& p, const CUtensorMap& tmap, int MB, cons
   }
 }
 
-// Stream-K scratch: per device, allocated once (never while the stream is
-// being captured) and never freed, so captured graphs keep valid pointers. A
-// ring of kSkRing slots (arrival counters + partial sums) is handed out round
-// robin, so up to kSkRing calls may run at once on one device.
-constexpr int kSkRing = 4;
+// Stream-K scratch (arrival counters + partial sums): one buffer per (device,
+// stream), allocated on first use outside stream capture and never freed, so
+// captured graphs keep valid pointers. Calls on one stream are ordered (also
+// with programmatic dependent launch: every use of the scratch follows the
+// kernel's griddepcontrol.wait), so they never share it concurrently.
 constexpr int kSkMinUnits = 6;
 constexpr int kSkAutoUnits = 48;
 constexpr int kSkMaxCounters = 16384;  // m-chunks x column tiles per call
-constexpr int kSkMaxDevices = 64;
-std::mutex g_sk_mu;
-void* g_sk_base[kSkMaxDevices];
-size_t g_sk_part_bytes[kSkMaxDevices];
-std::atomic<unsigned int> g_sk_seq{0};
 std::atomic<int> g_stream_k{1};
 
 bool stream_k_scratch(cudaStream_t st, int grid_max, bool may_alloc, int32_t** part, unsigned int** ctr) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kSkMaxDevices) return false;
-  std::lock_guard<std::mutex> lk(g_sk_mu);
-  if (!g_sk_base[dev]) {
-    if (!may_alloc) return false;
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return false;
-    const size_t part_bytes = (size_t)grid_max * 2 * kTileN * 32 * sizeof(int32_t);
-    const size_t slot = (size_t)kSkMaxCounters * 4 + part_bytes;
-    void* b = nullptr;
-    if (cudaMalloc(&b, slot * kSkRing) != cudaSuccess) {
-      cudaGetLastError();
-      return false;
-    }
-    if (cudaMemset(b, 0, slot * kSkRing) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
-      cudaFree(b);
-      cudaGetLastError();
-      return false;
-    }
-    g_sk_base[dev] = b;
-    g_sk_part_bytes[dev] = part_bytes;
-  }
-  if ((size_t)grid_max * 2 * kTileN * 32 * sizeof(int32_t) > g_sk_part_bytes[dev]) return false;
-  const unsigned int i = g_sk_seq.fetch_add(1u) % kSkRing;
-  char* s = static_cast<char*>(g_sk_base[dev]) + (size_t)i * ((size_t)kSkMaxCounters * 4 + g_sk_part_bytes[dev]);
+  if (!may_alloc) return false;
+  const size_t part_bytes = (size_t)grid_max * 2 * kTileN * 32 * sizeof(int32_t);
+  char* s = static_cast<char*>(stream_scratch(st, (size_t)kSkMaxCounters * 4 + part_bytes, 0));
+  if (!s) return false;
   *ctr = reinterpret_cast<unsigned int*>(s);
   *part = reinterpret_cast<int32_t*>(s + (size_t)kSkMaxCounters * 4);
   return true;
@@ -1037,7 +1020,11 @@ bool gemv_last_used_decode() { return t_used_decode; }
 cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaStream_t stream) {
   // shapes that fit one balanced wave (decode sizes) take the one-CTA-per-SM kernel
   t_used_decode = splits == 0 && g_stream_k.load() != 2 && decode_applicable(p, a_type, fmt);
-  if (t_used_decode) return launch_decode(p, a_type, fmt, stream);
+  if (t_used_decode) {
+    const cudaError_t e = launch_decode(p, a_type, fmt, stream);
+    if (e != cudaErrorNotSupported) return e;
+    t_used_decode = false;  // the shape needs the pre-pass, which had no scratch: split-K kernels instead
+  }
   // Every column tile stages and quantises its own copy of the activations;
   // when that repeated work is large (many tiles, M >= 16) the activations are
   // quantised once by a pre-pass and the kernel copies int8 rows instead.

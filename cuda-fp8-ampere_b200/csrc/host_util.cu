@@ -3,7 +3,10 @@
 #include "fp8imma_kernels.h"
 
 #include <cuda.h>
+#include <map>
 #include <mutex>
+#include <tuple>
+#include <vector>
 
 namespace fp8imma_b200 {
 
@@ -38,6 +41,50 @@ cudaError_t make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, 
                         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// Per-(device, stream, tag) scratch buffers, allocated on first use and grown
+// when a larger one is asked for; a buffer is handed only to work on its own
+// stream, so stream order keeps calls from overlapping on it. Buffers are
+// never freed (a replaced one may still be referenced by a captured graph).
+namespace {
+std::mutex g_scratch_mu;
+std::map<std::tuple<int, cudaStream_t, int>, std::pair<void*, size_t>> g_scratch;
+std::vector<void*> g_scratch_retired;
+}  // namespace
+
+void* stream_scratch(cudaStream_t stream, size_t bytes, int tag, bool* fresh) {
+  if (fresh) *fresh = false;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  auto key = std::make_tuple(dev, stream, tag);
+  auto it = g_scratch.find(key);
+  if (it != g_scratch.end() && it->second.second >= bytes) return it->second.first;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return nullptr;  // no allocation while a graph is being captured
+  }
+  size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+  void* p = nullptr;
+  if (cudaMalloc(&p, want) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (cudaMemset(p, 0, want) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(p);
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (fresh) *fresh = true;
+  if (it != g_scratch.end()) {
+    g_scratch_retired.push_back(it->second.first);
+    it->second = std::make_pair(p, want);
+  } else {
+    g_scratch.emplace(key, std::make_pair(p, want));
+  }
+  return p;
 }
 
 }  // namespace fp8imma_b200

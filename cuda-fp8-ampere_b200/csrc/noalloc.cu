@@ -98,7 +98,8 @@ extern "C" int fp8imma_gemm_rowquant_noalloc(const fp8imma_gemm_args* a, void* s
   p.out_row_major = a->out_layout;
   const bool fast = a->K > 0 && (a->K % 16) == 0 && (reinterpret_cast<uintptr_t>(a->A) & 15u) == 0 &&
                     (reinterpret_cast<uintptr_t>(a->B) & 15u) == 0;
-  p.no_alloc = 1;  // stream-K only when its scratch already exists
-  if (fast) return (int)launch_gemv_s8(p, a->a_type, a->b_format, 0, st);
+  p.no_alloc = 1;       // no pre-pass and no stream-K scratch (both allocate)
+  p.pdl = api_pdl();    // the process-wide knobs apply here as in fp8imma_gemm
+  if (fast) return (int)launch_gemv_s8(p, a->a_type, a->b_format, api_splitk(), st);
   return (int)launch_generic_s8(p, a->a_type, a->b_format, st);
 }

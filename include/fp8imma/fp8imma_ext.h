@@ -108,7 +108,10 @@ int fp8imma_quantize_weights(const void* W, int w_type, int N, int K, int fmt, v
 // device current); make that first call before any stream capture. Every call
 // on a device shares the one array (each call overwrites the rows it uses
 // before reading them), so calls that overlap on the GPU, e.g. on two streams
-// at once, race and must not be issued.
+// at once, race and must not be issued. fp8imma_set_pdl and fp8imma_set_splitk
+// apply as for fp8imma_gemm. Every M runs the small-M kernels (split-K /
+// decode; the tensor-core path needs scratch), so M in the hundreds or
+// thousands is correct but far slower than through fp8imma_gemm.
 int fp8imma_gemm_rowquant_noalloc(const fp8imma_gemm_args* args, void* stream);
 
 // fp8wgt linear: C[M,N] (fp32, row-major) = A[M,K] (fp16) x decode(B[N,K])^T,

@@ -18,11 +18,37 @@ def stream_ptr():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
+# Guard bands: an output tensor is the middle of a larger buffer whose first
+# and last GUARD elements hold a canary pattern; a kernel that writes outside
+# its output (a stray index, a wrong stride) changes them.
+GUARD = 4096
+CANARY = 0x5A5A
+_guards = {}
+
+
+def guarded(rows: int, cols: int, dtype=torch.float16, device="cuda") -> torch.Tensor:
+    """[rows, cols] 16-bit tensor (NaN-filled) between two canary bands."""
+    n = rows * cols
+    raw = torch.full((n + 2 * GUARD,), CANARY, dtype=torch.int16, device=device)
+    body = raw[GUARD:GUARD + n]
+    body.fill_(0x7E00 if dtype == torch.float16 else 0x7FC0)  # quiet NaN
+    t = body.view(dtype).view(rows, cols)
+    _guards[t.data_ptr()] = raw
+    return t
+
+
+def guards_intact(t: torch.Tensor) -> bool:
+    raw = _guards.pop(t.data_ptr())
+    torch.cuda.synchronize()
+    return bool((raw[:GUARD] == CANARY).all()) and bool((raw[-GUARD:] == CANARY).all())
+
+
 def cabi_ref_launch(name: str, kChunk: int, A, B, scales, M, N, K, gs, ainv=None, D=None):
-    """Call a reference-API C entry point; returns (err, D[N,M] fp16)."""
+    """Call a reference-API C entry point; returns (err, D[N,M] fp16). A D
+    allocated here sits between guard bands (check with guards_intact)."""
     L = F.lib()
     if D is None:
-        D = torch.full((N, M), float("nan"), dtype=torch.float16, device=A.device)
+        D = guarded(N, M, device=A.device)
     f = getattr(L, name)
     if ainv is None:
         err = f(kChunk, ptr(A), ptr(B), ptr(scales), ptr(D), M, N, K, float(gs), stream_ptr())

@@ -13,7 +13,7 @@ import torch
 
 import fp8imma_b200 as F
 from fp8imma_b200 import workloads as WL
-from helpers import bits_equal, to_np_bits
+from helpers import bits_equal, guarded, guards_intact, to_np_bits
 from oracle import oracle as O
 from test_gpu_ext import _epilogue_ref, inputs
 from test_gpu_parity import run_case
@@ -23,10 +23,11 @@ pytestmark = pytest.mark.gpu
 DECODE_PATH = 6
 
 # (M, N, K): the 4096^2 decode shapes (7 / 6 groups per CTA pair), a 70B-style
-# shard width (N = 3584), K not a multiple of 128 or 64, N not a multiple of 8, fewer
-# groups than SMs, K = 128 (no pair: one CTA per cluster), M = 9..15 (rows 8..15
+# shard (N = 3584, K = 8192; it fits only with the activation pre-pass of
+# M >= 8), K not a multiple of 128 or 64, N not a multiple of 8, fewer groups
+# than SMs, K = 128 (no pair: one CTA per cluster), M = 9..15 (rows 8..15
 # partly live)
-SHAPES = [(1, 4096, 4096), (16, 4096, 4096), (4, 4096, 4096), (16, 3584, 4096), (3, 200, 528), (9, 1003, 1040),
+SHAPES = [(1, 4096, 4096), (16, 4096, 4096), (4, 4096, 4096), (16, 3584, 8192), (3, 200, 528), (9, 1003, 1040),
           (16, 8, 256), (2, 24, 4160), (12, 7168, 1024), (8, 513, 128), (15, 1200, 2112)]
 
 
@@ -43,11 +44,13 @@ def _gemm(A, B, s, sig, M, N, K, a_bf16=False, fmt="e4m3", row_quant=False, bias
     e = F.ext()
     dA = torch.from_numpy(A.view(np.int16)).cuda().view(torch.bfloat16 if a_bf16 else torch.float16)
     kw = {} if bias is None else dict(bias=torch.from_numpy(bias).cuda(), act=act)
+    out = guarded(M, N, torch.bfloat16) if a_bf16 else guarded(N, M)  # bf16 tests use the row-major layout
     D, acc = e.imma_fp8_gemm(dA, torch.from_numpy(B).cuda(), torch.from_numpy(s.view(np.int16)).cuda(),
                              torch.from_numpy(sig).cuda(), 0.05, 20.0, "row" if row_quant else "tensor", fmt, "int8",
-                             "bfloat16" if a_bf16 else "float16", "row" if a_bf16 else "col", True, None, **kw)
+                             "bfloat16" if a_bf16 else "float16", "row" if a_bf16 else "col", True, out, **kw)
     path = e.last_path()
     torch.cuda.synchronize()
+    assert guards_intact(out), "writes outside the output"
     return D, acc, path
 
 
@@ -125,8 +128,9 @@ def test_decode_equals_split_k_kernel_graph_replay(decode_on, M, pdl):
     outs = [torch.empty(N, M, dtype=torch.float16, device="cuda") for _ in range(10)]
     st = torch.cuda.Stream()
     g = torch.cuda.CUDAGraph()
-    e.imma_fp8_gemm(inp.A, inp.B, inp.scales_u16, None, 1.0 / 16, 16.0, "tensor", "e4m3", "int8", "float16", "col",
-                    False, outs[0])
+    with torch.cuda.stream(st):  # first call on the capture stream: its scratch exists before capture
+        e.imma_fp8_gemm(inp.A, inp.B, inp.scales_u16, None, 1.0 / 16, 16.0, "tensor", "e4m3", "int8", "float16",
+                        "col", False, outs[0])
     assert e.last_path() == DECODE_PATH
     torch.cuda.synchronize()
     with torch.cuda.graph(g, stream=st):

@@ -8,7 +8,7 @@ import pytest
 import torch
 
 import fp8imma_b200 as F
-from helpers import bits_equal, cabi_ref_launch, ptr, stream_ptr, to_np_bits
+from helpers import bits_equal, cabi_ref_launch, guards_intact, ptr, stream_ptr, to_np_bits
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -65,6 +65,7 @@ def run_case(variant, M, N, K, seed=0, scale_mode="normal", codes="uniform", kch
     torch.cuda.synchronize()
     eq = bits_equal(to_np_bits(D), D_o)
     assert eq.all(), "%s M=%d N=%d K=%d: %d / %d mismatches" % (variant, M, N, K, (~eq).sum(), eq.size)
+    assert guards_intact(D), "writes outside the output"
 
 
 @pytest.mark.parametrize("variant", list(REF_FUNCS))

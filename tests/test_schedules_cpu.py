@@ -108,3 +108,51 @@ def test_tc_half_tail_items_cover_every_tile_once(tiles_w, tiles_x):
     # the half-width items of the last round fit in one round of pairs
     if n_full < ntiles:
         assert nwork - (nwork // maxpairs) * maxpairs <= maxpairs and 2 * (ntiles - n_full) <= maxpairs
+
+
+# ---- decode kernel: column groups per cluster, K split (decode.cu) ----------
+
+def decode_groups(NG, P):
+    """cg0 / G of every cluster, as the kernel computes them."""
+    return [(pc * NG // P, (pc + 1) * NG // P - pc * NG // P) for pc in range(P)]
+
+
+@pytest.mark.parametrize("N", [8, 24, 513, 1003, 3584, 4096, 7168, 11008])
+@pytest.mark.parametrize("P", [1, 25, 74, 148])
+def test_decode_groups_cover_every_column_once(N, P):
+    NG = (N + 7) // 8
+    P = min(P, NG)
+    gs = decode_groups(NG, P)
+    sizes = [g for _, g in gs]
+    assert sum(sizes) == NG
+    assert max(sizes) - min(sizes) <= 1  # balanced to within one group
+    nxt = 0
+    for cg0, g in gs:
+        assert cg0 == nxt
+        nxt += g
+
+
+# ---- fused NVLink gather: per-call counter shares (gemv_splitk.cu) ----------
+
+U_CALL = 1 << 20
+
+
+def gather_share(i, n):
+    return (i + 1) * U_CALL // n - i * U_CALL // n
+
+
+def test_fused_gather_target_alignment_with_alternating_shapes():
+    """Every call adds exactly U to each peer counter whatever its cluster
+    count, so after e calls of any mix of shapes the counter equals e * U
+    (mod 2^32) and the waiting CTA's target stays aligned."""
+    rng = random.Random(3)
+    ctr = 0
+    for e in range(1, 3000):
+        clusters = rng.choice([1, 3, 32, 224, 256, 1000, 16384])
+        add = sum(gather_share(i, clusters) for i in range(clusters))
+        assert add == U_CALL
+        assert all(gather_share(i, clusters) > 0 for i in (0, clusters - 1))
+        ctr = (ctr + add) % (1 << 32)
+        target = (e * U_CALL) % (1 << 32)
+        diff = (ctr - target) % (1 << 32)
+        assert diff == 0

@@ -17,6 +17,8 @@ import torch
 
 import fp8imma_b200 as F
 from helpers import ptr, stream_ptr, bits_equal, to_np_bits
+from oracle import oracle as O
+from test_gpu_ext import inputs
 
 pytestmark = pytest.mark.gpu
 
@@ -68,3 +70,25 @@ def test_noalloc_rejects_too_many_rows(cuda):
     D = torch.empty(N, M, dtype=torch.float16, device="cuda")
     a = make_args(A, B, s16, D, M, N, K, False)
     assert L.fp8imma_gemm_rowquant_noalloc(ctypes.byref(a), stream_ptr()) == 1  # cudaErrorInvalidValue
+
+
+@pytest.mark.parametrize("M,N,K", [(65, 96, 256), (1024, 64, 128), (4096, 32, 128), (12, 200, 1000)])
+def test_noalloc_matches_oracle(cuda, M, N, K):
+    """Against the CPU oracle's per-row quantisation directly (not only against
+    the allocating entry): M above the small-M range, where this entry still
+    runs the split-K kernel, and K = 1000 (not a multiple of 16: the generic
+    kernel)."""
+    L = F.lib()
+    A, B, s, _ = inputs(M, N, K, seed=M + K)
+    dA = torch.from_numpy(A.view(np.int16)).cuda().view(torch.float16)
+    dB = torch.from_numpy(B).cuda()
+    ds = torch.from_numpy(s.view(np.int16)).cuda()
+    D = torch.full((N, M), float("nan"), dtype=torch.float16, device="cuda")
+    acc = torch.zeros(N, M, dtype=torch.int32, device="cuda")
+    a = make_args(dA, dB, ds, D, M, N, K, False, acc)
+    a.global_scale = 0.05
+    assert L.fp8imma_gemm_rowquant_noalloc(ctypes.byref(a), stream_ptr()) == 0
+    torch.cuda.synchronize()
+    D_o, acc_o = O.gemm_ex(A, B, s, row_quant=True, global_scale=0.05, nthreads=16)
+    assert (acc.cpu().numpy() == acc_o).all(), "int32 accumulators differ"
+    assert bits_equal(to_np_bits(D), D_o).all()
