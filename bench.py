@@ -204,6 +204,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-lib", action="store_true")
     ap.add_argument("--points", action="store_true", help="also time the other decode/70B shapes")
+    ap.add_argument("--no-metric-points", action="store_true",
+                    help="skip the metric's other M points (decode M=1, square M=4096) on the default line")
     ap.add_argument("--points-only", default="", help="comma-separated subset of the --points shapes")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--gather", default="peer", choices=["peer", "peer-epilogue", "nccl"],
@@ -433,6 +435,8 @@ def main():
     extra = {}
     if rank == 0 and world == 1 and not args.no_ref_lib:
         extra["ref_lib_b200"] = time_reference_lib(A, Bs, s16, M, Nl, K, gs, ainv, args.steps, copies)
+    if rank == 0 and world == 1 and not args.no_metric_points:
+        extra["metric_points"] = time_metric_points(ext, local, hbm, bf16, peak_kind)
     if rank == 0 and world == 1 and args.points:
         extra["points"] = time_points(ext, args.steps, [x for x in args.points_only.split(",") if x])
 
@@ -502,6 +506,92 @@ def time_reference_lib(A, Bs, s16, M, N, K, gs, ainv, steps, copies):
     ms = ev0.elapsed_time(ev1) / n
     return {"value": round(alg_bytes(M, N, K) / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_call": round(ms, 5),
             "timing": "eager launches, CUDA events"}
+
+
+def _timed_graph(call, n_calls, gpu_index, min_ms):
+    """CUDA graph of n_calls calls (warmed up on the capture stream); the GPU
+    is kept busy ~0.6 s while nvidia-smi samples the clocks, then the graph is
+    replayed until at least min_ms of device time is timed. Returns
+    (ms per call, clocks)."""
+    import torch
+
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        for i in range(3):
+            call(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for i in range(n_calls):
+            call(i)
+    g.replay()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    g.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    reps = max(1, int(math.ceil(min_ms / max(ev0.elapsed_time(ev1), 1e-3))))
+    sampler = ClockSampler(gpu_index)
+    sampler.start()
+    t_end = time.time() + 0.6
+    while time.time() < t_end:
+        g.replay()
+        torch.cuda.synchronize()
+    ev0.record()
+    for _ in range(reps):
+        g.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    return ev0.elapsed_time(ev1) / (reps * n_calls), clocks
+
+
+def time_metric_points(ext, gpu_index, hbm, bf16, peak_kind):
+    """The metric's other M points on one GPU, each with its own roofline and
+    clock record: decode M=1 (N=K=4096, HBM-bound, weights rotated over > 2x
+    L2), decode M=16 with per-row activation quantisation, and the square
+    M=N=K=4096 GEMM (tensor-bound, >= 50 ms timed)."""
+    import torch
+
+    from fp8imma_b200 import workloads as WL
+
+    out = {}
+    for name, (M, N, K, dist_, outl, n_calls, min_ms, aq) in {
+            "decode_m1": (1, 4096, 4096, "normal", 0.01, 500, 5.0, "tensor"),
+            "decode_m16_rowquant": (16, 4096, 4096, "normal", 0.01, 500, 5.0, "row"),
+            "square4096": (4096, 4096, 4096, "uniform4", 0.0, 20, 50.0, "tensor")}.items():
+        B, s16, _ = WL.make_weights(N, K, 0.02, "e4m3", seed=0)
+        A = WL.make_activations(M, K, dist_, outl, seed=1)
+        l2 = torch.cuda.get_device_properties(A.device).L2_cache_size
+        copies = max(1, math.ceil(2 * l2 / B.numel())) + 1 if B.numel() < 2 * l2 else 1
+        Bs = [B] + [B.clone() for _ in range(copies - 1)]
+        D = torch.empty(N, M, dtype=torch.float16, device=A.device)
+
+        def call(i):
+            ext.imma_fp8_gemm(A, Bs[i % copies], s16, None, 1.0 / 16, 16.0, aq, "e4m3", "int8", "float16",
+                              "col", False, D)
+
+        ms, clocks = _timed_graph(call, n_calls, gpu_index, min_ms)
+        path = ext.last_path()
+        if M > 64:
+            achieved = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+            roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": 2.0 * bf16, "unit": "TFLOP/s",
+                    "frac": round(achieved / (2.0 * bf16), 4),
+                    "peak_source": "2 x MEASURED_PEAKS.json bf16_tflops (%s)" % peak_kind}
+            val, unit = achieved, "TFLOPS"
+        else:
+            achieved = alg_bytes(M, N, K) / (ms * 1e-3) / 1e9
+            roof = {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm, "unit": "GB/s",
+                    "frac": round(achieved / hbm, 4), "peak_source": "MEASURED_PEAKS.json hbm_gbs (%s)" % peak_kind}
+            val, unit = achieved, "GB/s"
+        out[name] = {"M": M, "N": N, "K": K, "act_quant": aq, "us": round(ms * 1e3, 3), "value": round(val, 2),
+                     "unit": unit,
+                     "roofline": roof, "clocks": clocks, "kernel_path": path,
+                     "timing": "CUDA graph of %d calls, >= %g ms timed" % (n_calls, min_ms)}
+        del Bs, B, A, D
+        torch.cuda.empty_cache()
+    return out
 
 
 def time_points(ext, steps, only=None):

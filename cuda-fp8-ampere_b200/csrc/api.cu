@@ -30,6 +30,8 @@ int g_dbg = 0;
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+
+
 enum { FMT_E4M3_REF = 0, FMT_E5M2 = 1 };
 }  // namespace
 
@@ -81,12 +83,12 @@ static cudaError_t run_int8(GemvParams p, int a_type, int fmt, int group, cudaSt
 #endif
   const bool fast_shape = p.K > 0 && (p.K % 16) == 0 && aligned16(p.A) && aligned16(p.B);
   if (fast_shape && p.M > g_small_m_max.load()) {
-    void* scratch = nullptr;
-    cudaError_t e = cudaMallocAsync(&scratch, gemm_tc_scratch_bytes(p.M, p.N, p.K, false), stream);
+    ScopedScratch sc;
+    cudaError_t e = sc.get(gemm_tc_scratch_bytes(p.M, p.N, p.K, false), stream, kScratchTc);
     if (e != cudaSuccess) return e;
     t_last_path = 3;
-    e = launch_gemm_tc_s8(p, a_type, fmt, scratch, stream);
-    cudaError_t e2 = cudaFreeAsync(scratch, stream);
+    e = launch_gemm_tc_s8(p, a_type, fmt, sc.ptr, stream);
+    cudaError_t e2 = sc.release(stream);
     return e != cudaSuccess ? e : e2;
   }
   if (fast_shape) {
@@ -140,9 +142,10 @@ static cudaError_t gemm_native(const fp8imma_gemm_args* a, cudaStream_t stream) 
       a->out_layout > 1)
     return cudaErrorInvalidValue;
   if ((a->K % 16) != 0 || !aligned16(a->A) || !aligned16(a->B)) return cudaErrorInvalidValue;
-  void* scratch = nullptr;
-  cudaError_t e = cudaMallocAsync(&scratch, gemm_tc_scratch_bytes(a->M, a->N, a->K, true), stream);
+  ScopedScratch sc;
+  cudaError_t e = sc.get(gemm_tc_scratch_bytes(a->M, a->N, a->K, true), stream, kScratchTc);
   if (e != cudaSuccess) return e;
+  void* scratch = sc.ptr;
   if (a->M <= g_small_m_max.load()) {
     // small M: per-row E4M3 activations, then the split-K kernel with FP8 tensor-core MMAs
     uint8_t* Aq = static_cast<uint8_t*>(scratch);
@@ -172,7 +175,7 @@ static cudaError_t gemm_native(const fp8imma_gemm_args* a, cudaStream_t stream) 
     e = launch_gemm_tc_fp8(a->A, a->a_type, static_cast<const uint8_t*>(a->B), a->b_format, a->col_scales_f32,
                            a->D, a->M, a->N, a->K, a->out_type, a->out_layout, scratch, stream, t_bias, t_act);
   }
-  cudaError_t e2 = cudaFreeAsync(scratch, stream);
+  cudaError_t e2 = sc.release(stream);
   return e != cudaSuccess ? e : e2;
 }
 
@@ -197,11 +200,24 @@ static cudaError_t gemm_ex(const fp8imma_gemm_args* a, cudaStream_t stream) {
   if (a->act_quant == FP8IMMA_AQ_ROW) {
     if (a->M <= 0 || a->N <= 0) return cudaErrorInvalidConfiguration;
     if (!a->A || a->K < 0) return cudaErrorInvalidValue;
-    void* tmp = nullptr;
+    // decode shapes: row scales and quantisation in one pre-pass before the decode kernel
+    if (a->K > 0 && (a->K % 16) == 0 && aligned16(a->A) && aligned16(a->B) && a->M <= g_small_m_max.load() &&
+        g_splitk.load() == 0) {
+      GemvParams q = p;
+      q.pdl = g_pdl.load();
+      if (decode_applicable(q, a->a_type, a->b_format)) {
+        const cudaError_t e = launch_decode_rowquant(q, a->a_type, a->b_format, stream);
+        if (e != cudaErrorNotSupported) {
+          t_last_path = 6;
+          return e;
+        }
+      }
+    }
+    ScopedScratch sc;
     size_t bytes = (size_t)a->M * (sizeof(float) + sizeof(uint16_t)) + 16;
-    cudaError_t e = cudaMallocAsync(&tmp, bytes, stream);
+    cudaError_t e = sc.get(bytes, stream, kScratchRowScales);
     if (e != cudaSuccess) return e;
-    float* g = static_cast<float*>(tmp);
+    float* g = static_cast<float*>(sc.ptr);
     uint16_t* inv = reinterpret_cast<uint16_t*>(g + a->M);
     e = launch_row_scales(a->A, a->a_type, a->M, a->K, inv, g, stream);
     if (e == cudaSuccess) {
@@ -209,7 +225,7 @@ static cudaError_t gemm_ex(const fp8imma_gemm_args* a, cudaStream_t stream) {
       p.row_g = g;
       e = run_int8(p, a->a_type, a->b_format, group, stream);
     }
-    cudaError_t e2 = cudaFreeAsync(tmp, stream);
+    cudaError_t e2 = sc.release(stream);
     return e != cudaSuccess ? e : e2;
   }
   return run_int8(p, a->a_type, a->b_format, group, stream);

@@ -641,6 +641,64 @@ __global__ void __launch_bounds__(256) dec_quant_kernel(const void* __restrict__
   }
 }
 
+// Per-row variant of the pre-pass: one CTA per row computes the row's absolute
+// maximum (fp16 values; bf16 rounded to fp16 first), its multiplier
+// fp16(127 / amax) and output scale 1 / (127 / amax) exactly as the row-scale
+// kernel does (amax 0 or not finite: both 0), and quantises the row with it.
+template <int AT>
+__global__ void __launch_bounds__(256) dec_rowquant_kernel(const void* __restrict__ A, int K,
+                                                           int8_t* __restrict__ Aq, uint16_t* __restrict__ a_inv_h,
+                                                           float* __restrict__ g) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ float red[8];
+  __shared__ uint32_t inv_s;
+  const int m = blockIdx.x;
+  const uint4* row = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(A) + (size_t)m * K);
+  uint2* out = reinterpret_cast<uint2*>(Aq + (size_t)m * K);
+  const int items = K >> 3;
+  float amax = 0.0f;
+  for (int i = threadIdx.x; i < items; i += blockDim.x) {
+    uint4 v = row[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t h2 = AT == A_BF16 ? bf16x2_to_f16x2(w[j]) : w[j];
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+      amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) a = fmaxf(a, red[w]);
+    float inv = 0.0f, gg = 0.0f;
+    if (a > 0.0f && a <= 3.402823466e38f) {
+      inv = __fdiv_rn(127.0f, a);
+      gg = __fdiv_rn(1.0f, inv);
+    }
+    const uint16_t ih = __half_as_ushort(__float2half_rn(inv));
+    a_inv_h[m] = ih;
+    g[m] = gg;
+    inv_s = (uint32_t)ih | ((uint32_t)ih << 16);
+  }
+  __syncthreads();
+  const uint32_t ainv2 = inv_s;
+  for (int i = threadIdx.x; i < items; i += blockDim.x) {  // second read: L1 / L2 resident
+    uint4 v = row[i];
+    if (AT == A_BF16) {
+      v.x = bf16x2_to_f16x2(v.x);
+      v.y = bf16x2_to_f16x2(v.y);
+      v.z = bf16x2_to_f16x2(v.z);
+      v.w = bf16x2_to_f16x2(v.w);
+    }
+    out[i] = make_uint2(quant4_f16(v.x, v.y, ainv2), quant4_f16(v.z, v.w, ainv2));
+  }
+}
+
 std::atomic<int> g_decode_mode{1};
 constexpr int kDecPrepassM = 1;  // rows from which the pre-pass beats per-CTA quantisation
 
@@ -802,6 +860,38 @@ cudaError_t launch_decode(const GemvParams& p_in, int a_type, int fmt, cudaStrea
     case A_S8 * 8 + 1: return dec_launch<A_S8, FMT_E5M2>(p, tf, ts, ta, cfg, smem, stream);
     default: return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t launch_decode_rowquant(const GemvParams& p_in, int a_type, int fmt, cudaStream_t stream) {
+  if (a_type != A_F16 && a_type != A_BF16) return cudaErrorNotSupported;
+  GemvParams p = p_in;
+  p.row_quant = 0;
+  DecodeCfg cfg;
+  size_t smem;
+  if (p.no_alloc || !decode_plan(p.M, p.N, p.K, 1, num_sms_current(), &cfg, &smem)) return cudaErrorNotSupported;
+  const size_t rows_bytes = ((size_t)p.M * p.K + 255) & ~size_t(255);
+  uint8_t* sc = static_cast<uint8_t*>(stream_scratch(stream, rows_bytes + (size_t)p.M * 8 + 256, 1));
+  if (!sc) return cudaErrorNotSupported;
+  int8_t* aq = reinterpret_cast<int8_t*>(sc);
+  float* g = reinterpret_cast<float*>(sc + rows_bytes);
+  uint16_t* inv = reinterpret_cast<uint16_t*>(g + p.M);
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3((unsigned)p.M, 1, 1);
+  lc.blockDim = dim3(256, 1, 1);
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  cudaError_t e = a_type == A_BF16 ? cudaLaunchKernelEx(&lc, dec_rowquant_kernel<A_BF16>, p.A, p.K, aq, inv, g)
+                                   : cudaLaunchKernelEx(&lc, dec_rowquant_kernel<A_F16>, p.A, p.K, aq, inv, g);
+  if (e != cudaSuccess) return e;
+  p.A = aq;
+  p.row_inv_h = nullptr;
+  p.row_g = g;
+  p.pdl = 1;  // weights stream while the pre-pass runs; rows and row scales are read after it
+  return launch_decode(p, A_S8, fmt, stream);
 }
 
 void decode_set_mode(int mode) { g_decode_mode.store(mode); }

@@ -35,6 +35,7 @@ struct GemvParams {
   float wgt_scale;                  // FMT_WGT: scale_b (or scale_b / 256 when wgt_fast)
   int wgt_fast;                     // FMT_WGT: packed decode allowed for this scale
   int no_alloc;                     // the launcher may not allocate device memory
+  int row_quant;                    // per-row scales still to be computed (decode pre-pass)
   const float* bias;                // optional fused epilogue: + bias[n] (fp32)
   int act;                          // then 0 none, 1 ReLU, 2 GELU (tanh), 3 SiLU
   // column-parallel gather fused into the split-K epilogue (world > 1)
@@ -63,8 +64,27 @@ int api_splitk();
 // use (zero-filled) and grown on demand, never freed; nullptr while the
 // stream is capturing a graph and no large enough buffer exists yet (callers
 // then take a path without scratch). *fresh tells whether the buffer was just
-// (re)allocated. Tags: 0 stream-K partials, 1 decode activation rows.
+// (re)allocated. Tags: 0 stream-K partials, 1 decode activation rows,
+// 2 tensor-core prep operands, 3 per-row activation scales.
 void* stream_scratch(cudaStream_t stream, size_t bytes, int tag, bool* fresh = nullptr);
+
+// Temporary device memory of one call: the calling stream's own scratch buffer
+// (allocated once per device and stream, outside graph capture, and reused by
+// every later call on that stream), or, while a graph is being captured before
+// that buffer exists, a stream-ordered allocation freed at the end of the call.
+struct ScopedScratch {
+  void* ptr = nullptr;
+  bool owned = false;
+  cudaError_t get(size_t bytes, cudaStream_t st, int tag) {
+    ptr = stream_scratch(st, bytes, tag);
+    if (ptr) return cudaSuccess;
+    owned = true;
+    return cudaMallocAsync(&ptr, bytes, st);
+  }
+  cudaError_t release(cudaStream_t st) { return owned && ptr ? cudaFreeAsync(ptr, st) : cudaSuccess; }
+};
+// Tags of the callers of ScopedScratch
+enum { kScratchTc = 2, kScratchRowScales = 3, kScratchGemvRows = 4, kScratchWgt = 5 };
 
 // TMA descriptor for a 2-D byte tensor [outer][inner] (row pitch row_bytes).
 cudaError_t make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
@@ -95,6 +115,11 @@ void gemv_set_stream_k(int mode);
 // per CTA. decode_set_mode(0) turns it off (the split-K kernels run instead).
 bool decode_applicable(const GemvParams& p, int a_type, int fmt);
 cudaError_t launch_decode(const GemvParams& p, int a_type, int fmt, cudaStream_t stream);
+// Per-row quantised decode in two launches: one pre-pass computes each row's
+// scales (as launch_row_scales) and quantises the row, then the decode kernel.
+// cudaErrorNotSupported when the shape or the stream's scratch does not allow
+// it (the caller then takes the row-scale kernel + GEMM route).
+cudaError_t launch_decode_rowquant(const GemvParams& p, int a_type, int fmt, cudaStream_t stream);
 void decode_set_mode(int mode);
 
 // Large-M tensor-core path (tcgen05). Scratch must hold

@@ -121,12 +121,12 @@ extern "C" int fp8imma_fp8wgt_linear_forward(const void* A, const void* B, float
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (M > 64 && (reinterpret_cast<uintptr_t>(B) & 15u) == 0) {
     // large M: weights decoded once to fp16, then tcgen05 kind::f16 (fp32 accumulate)
-    void* scratch = nullptr;
+    ScopedScratch sc;
     const size_t ws = tc_splitk_ws_bytes(M, N, 2 * K);  // split-K accumulators for mid-size M
-    cudaError_t e = cudaMallocAsync(&scratch, (((size_t)N * K * 2 + 255) & ~size_t(255)) + ws, st);
+    cudaError_t e = sc.get((((size_t)N * K * 2 + 255) & ~size_t(255)) + ws, st, kScratchWgt);
     if (e != cudaSuccess) return (int)e;
-    e = launch_gemm_tc_wgt(A, static_cast<const uint8_t*>(B), scale_b, static_cast<float*>(C), M, N, K, scratch, st);
-    cudaError_t e2 = cudaFreeAsync(scratch, st);
+    e = launch_gemm_tc_wgt(A, static_cast<const uint8_t*>(B), scale_b, static_cast<float*>(C), M, N, K, sc.ptr, st);
+    cudaError_t e2 = sc.release(st);
     return (int)(e != cudaSuccess ? e : e2);
   }
   if ((reinterpret_cast<uintptr_t>(B) & 15u) == 0) {

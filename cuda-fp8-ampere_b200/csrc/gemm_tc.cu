@@ -28,9 +28,15 @@
 using namespace fp8imma_dev;
 
 // tensor-core GEMM waits park the thread (see mbar_try_wait)
-constexpr bool kTcSuspend = true;
+#ifndef FP8IMMA_TC_SUSPEND
+#define FP8IMMA_TC_SUSPEND 1
+#endif
+constexpr bool kTcSuspend = FP8IMMA_TC_SUSPEND != 0;
 
 namespace fp8imma_b200 {
+#ifdef FP8IMMA_TRACE
+static unsigned long long* g_tc_trace = nullptr;  // trace builds only
+#endif
 
 namespace {
 
@@ -136,6 +142,8 @@ struct TcParams {
   int splits;          // CTA-pair kernel: K splits per tile (1 = none)
   int kb_per_split;    // 128-byte K blocks per split
   uint32_t* ws;        // splits > 1: raw accumulators [split][n][m] (int32 or fp32 bits)
+  int tma_out;         // CTA-pair kernel: col-major 16-bit output written by TMA stores (mapD)
+  unsigned long long* trace;  // trace builds only: 64 words per CTA
 };
 
 template <int KIND>
@@ -282,6 +290,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           o[j] = store_val(bias_act(v, p.bias, n, p.act), p.out_bf16);
         }
         const int mcount = min(32, p.M - mbase);
+#ifdef FP8IMMA_TC_EPI_DBG
+        if (FP8IMMA_TC_EPI_DBG == 1) {
+          if (o[0] == 0x1234u && o[31] == 0x9u) D[0] = 1;
+          continue;
+        }
+#endif
         if (p.out_row_major) {
           _Pragma("unroll") for (int j = 0; j < 32; ++j) if (j < mcount) D[(size_t)(mbase + j) * p.N + n] = o[j];
         } else {
@@ -591,8 +605,21 @@ __device__ __forceinline__ TcItem tc_item(const TcParams& p, int wi) {
 template <int KIND>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     gemm_tc2_kernel(const __grid_constant__ TcParams p, const __grid_constant__ CUtensorMap mapW,
-                    const __grid_constant__ CUtensorMap mapX, const __grid_constant__ CUtensorMap mapXh) {
+                    const __grid_constant__ CUtensorMap mapX, const __grid_constant__ CUtensorMap mapXh,
+                    const __grid_constant__ CUtensorMap mapD) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+#ifdef FP8IMMA_TRACE
+  // per CTA 64 words, cycle counts since entry: [0] entry %globaltimer, [1] SM,
+  // [3..4] producer empty-wait cycles / end, [5..7] MMA tempty-wait, full-wait,
+  // end, [8..11] epilogue warp q=0: tfull-wait, tmem-load, work, end
+  const long long tr0 = clock64();
+  long long tr[16] = {0};
+#define TC_T0() const long long _t = clock64()
+#define TC_ACC(i) tr[i] += clock64() - _t
+#else
+#define TC_T0() do { } while (0)
+#define TC_ACC(i) do { } while (0)
+#endif
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages2 * kStageBytes2);
   uint64_t* empty = full + kStages2;
@@ -600,6 +627,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  // epilogue staging for TMA stores: 4 warps x 2 buffers x [32 columns][16 words]
+  uint32_t* epi_stage = reinterpret_cast<uint32_t*>(smem + kStages2 * kStageBytes2 + 256);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();  // 0 = leader (issues the MMAs)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
@@ -649,7 +678,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         const int kb0 = it.split * p.kb_per_split, kb1 = min(nkb, kb0 + p.kb_per_split);
         const CUtensorMap* mx = it.xw == p.tile_x ? &mapX : &mapXh;
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!(ok = mbar_wait<kTcSuspend>(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY))) break;
+          {
+            TC_T0();
+            ok = mbar_wait<kTcSuspend>(&empty[stage], phase ^ 1u, ERR_WAIT_EMPTY);
+            TC_ACC(3);
+          }
+          if (!ok) break;
           uint8_t* sw = smem + stage * kStageBytes2;
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (kHalfBytes + (it.xw >> 1) * kBK));
           const uint32_t fb = full_leader + stage * 8;
@@ -681,11 +715,21 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         const TcItem ti = tc_item(p, wi);
         const uint32_t idesc = ti.xw == p.tile_x ? p.idesc : p.idesc_half;
         const int kb0 = ti.split * p.kb_per_split, kb1 = min(nkb, kb0 + p.kb_per_split);
-        if (!(ok = mbar_wait<kTcSuspend>(&tempty[buf], ((it >> 1) & 1) ^ 1u, ERR_WAIT_TMEM_EMPTY))) break;
+        {
+          TC_T0();
+          ok = mbar_wait<kTcSuspend>(&tempty[buf], ((it >> 1) & 1) ^ 1u, ERR_WAIT_TMEM_EMPTY);
+          TC_ACC(5);
+        }
+        if (!ok) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * 256);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!(ok = mbar_wait<kTcSuspend>(&full[stage], phase, ERR_WAIT_FULL))) break;
+          {
+            TC_T0();
+            ok = mbar_wait<kTcSuspend>(&full[stage], phase, ERR_WAIT_FULL);
+            TC_ACC(6);
+          }
+          if (!ok) break;
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * kStageBytes2);
           const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + kHalfBytes);
@@ -707,11 +751,21 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     // ---- epilogue (both CTAs): this CTA's 128 TMEM lanes = 128 weight columns
     const int q = warp & 3;
     int it = 0;
+    int sbuf = 0;  // TMA-store staging buffer of this warp (two, alternating)
     for (int wi = pair; wi < nwork; wi += npairs, ++it) {
       const int buf = it & 1;
       const TcItem ti = tc_item(p, wi);
       const int tw = ti.tw, split = ti.split;
-      if (!mbar_wait<kTcSuspend>(&tfull[buf], (it >> 1) & 1, ERR_WAIT_TMEM_FULL)) break;
+      bool okw;
+      {
+        TC_T0();
+        okw = mbar_wait<kTcSuspend>(&tfull[buf], (it >> 1) & 1, ERR_WAIT_TMEM_FULL);
+        TC_ACC(8);
+      }
+      if (!okw) break;
+#ifdef FP8IMMA_TRACE
+      const long long tw0 = clock64();
+#endif
       tc_fence_after();
       const int n = tw * 256 + 128 * (int)rank + q * 32 + lane;
       const bool nok = n < p.N;
@@ -726,9 +780,71 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll 1
       for (int j0 = 0; j0 < ti.xw; j0 += 32) {
         uint32_t r[32];
-        tmem_ld32(taddr + j0, r);
+        {
+          TC_T0();
+          tmem_ld32(taddr + j0, r);
+          TC_ACC(9);
+        }
         const int mbase = ti.x0 + j0;
+        // col-major 16-bit output: the warp stages its 32 columns x 32 rows in
+        // shared memory and one lane writes the box with a TMA store (the
+        // tensor map clips rows past M and columns past N). Per-lane 16-byte
+        // stores, 32 columns 8 KB apart per instruction, ran at a fraction of
+        // the GEMM's speed.
+        if (p.tma_out) {
+          uint32_t* st = epi_stage + (q * 2 + sbuf) * 512;  // [32 columns][16 words] dense, 2 KB
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");  // this buffer's last store read it
+          __syncwarp();
+          uint32_t pk[16];
+#pragma unroll
+          for (int w2 = 0; w2 < 16; ++w2) {
+            const int m = mbase + 2 * w2;
+            float v0, v1;
+            if (KIND == KIND_I8) {
+              float se0 = cs * (p.row_g ? p.row_g[m < p.M ? m : 0] : p.global_scale);
+              float se1 = cs * (p.row_g ? p.row_g[m + 1 < p.M ? m + 1 : 0] : p.global_scale);
+              if (p.col_scale_f32) {
+                se0 = se0 * cs2;
+                se1 = se1 * cs2;
+              }
+              v0 = (float)(int32_t)r[2 * w2] * se0;
+              v1 = (float)(int32_t)r[2 * w2 + 1] * se1;
+            } else {
+              const float rs0 = p.row_g ? p.row_g[m < p.M ? m : 0] : 1.0f;
+              const float rs1 = p.row_g ? p.row_g[m + 1 < p.M ? m + 1 : 0] : 1.0f;
+              v0 = __uint_as_float(r[2 * w2]) * rs0 * cs2;
+              v1 = __uint_as_float(r[2 * w2 + 1]) * rs1 * cs2;
+            }
+            pk[w2] = (uint32_t)store_val(bias_act(v0, p.bias, nok ? n : 0, p.act), p.out_bf16) |
+                     ((uint32_t)store_val(bias_act(v1, p.bias, nok ? n : 0, p.act), p.out_bf16) << 16);
+          }
+          uint4* row4 = reinterpret_cast<uint4*>(st + lane * 16);
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) row4[v4] = make_uint4(pk[4 * v4], pk[4 * v4 + 1], pk[4 * v4 + 2], pk[4 * v4 + 3]);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> async-proxy reads
+          __syncwarp();
+          if (lane == 0 && mbase < p.M) {
+            asm volatile(
+                "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                    reinterpret_cast<uint64_t>(&mapD)),
+                "r"(mbase * 2), "r"(n - lane), "r"(smem_u32(st))
+                : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+          sbuf ^= 1;
+          if (KIND == KIND_I8 && p.acc_out && nok) {
+            const int mc = min(32, p.M - mbase);
+            _Pragma("unroll") for (int j = 0; j < 32; ++j) if (j < mc) p.acc_out[(size_t)n * p.M + mbase + j] = (int32_t)r[j];
+          }
+          continue;
+        }
         if (!nok || mbase >= p.M) continue;
+#ifdef FP8IMMA_TC_EPI_DBG
+        if (FP8IMMA_TC_EPI_DBG == 2) {
+          if (r[0] == 0x12345678u && r[31] == 0x9u) static_cast<uint16_t*>(p.D)[0] = 1;
+          continue;
+        }
+#endif
         if (p.splits > 1) {  // raw accumulators of this K split; tc_splitk_reduce_kernel finishes
           uint32_t* dst = p.ws + ((size_t)split * p.N + n) * p.M + mbase;
           const int mc = min(32, p.M - mbase);
@@ -763,6 +879,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           o[j] = store_val(bias_act(v, p.bias, n, p.act), p.out_bf16);
         }
         const int mcount = min(32, p.M - mbase);
+#ifdef FP8IMMA_TC_EPI_DBG
+        if (FP8IMMA_TC_EPI_DBG == 1) {
+          if (o[0] == 0x1234u && o[31] == 0x9u) D[0] = 1;
+          continue;
+        }
+#endif
         if (p.out_row_major) {
           _Pragma("unroll") for (int j = 0; j < 32; ++j) if (j < mcount) D[(size_t)(mbase + j) * p.N + n] = o[j];
         } else {
@@ -788,8 +910,34 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(tempty_leader + buf * 8);
+#ifdef FP8IMMA_TRACE
+      tr[10] += clock64() - tw0;
+#endif
+    }
+    if (p.tma_out && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // stores complete
+  }
+#ifdef FP8IMMA_TRACE
+  if (p.trace && lane == 0) {
+    unsigned long long* t = p.trace + (size_t)blockIdx.x * 64;
+    if (warp == 0) {
+      t[0] = globaltimer_ns();
+      uint32_t smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      t[1] = smid;
+      t[3] = tr[3];
+      t[4] = clock64() - tr0;
+    } else if (warp == 1) {
+      t[5] = tr[5];
+      t[6] = tr[6];
+      t[7] = clock64() - tr0;
+    } else if ((warp & 3) == 0) {
+      t[8] = tr[8];
+      t[9] = tr[9];
+      t[10] = tr[10];
+      t[11] = clock64() - tr0;
     }
   }
+#endif
 
   tc_fence_before();
   cluster_barrier();  // no CTA leaves while its pair may still use its smem or TMEM
@@ -902,8 +1050,19 @@ cudaError_t launch_tc2(TcParams p, const void* W, const void* X, int a_fmt, cuda
   p.tiles_x = (p.M + p.tile_x - 1) / p.tile_x;
   p.idesc = make_idesc2<KIND>(a_fmt, p.tile_x);
   p.idesc_half = make_idesc2<KIND>(a_fmt, p.tile_x / 2);
+  // col-major fp16 / bf16 output through TMA stores: rows of M * 2 bytes must
+  // be a multiple of 16 bytes and D 16-byte aligned
+  CUtensorMap md = mw;
+  p.tma_out = 0;
+#ifdef FP8IMMA_TRACE
+  p.trace = g_tc_trace;
+#endif
+  if (KIND != KIND_F16 && p.splits <= 1 && !p.out_row_major && (p.M % 8) == 0 &&
+      (reinterpret_cast<uintptr_t>(p.D) & 15u) == 0 &&
+      make_tmap_2d_u8(&md, p.D, (uint64_t)p.M * 2, p.N, (uint64_t)p.M * 2, 64, 32, false) == cudaSuccess)
+    p.tma_out = 1;
   auto kern = gemm_tc2_kernel<KIND>;
-  const int smem = kStages2 * kStageBytes2 + 1024 + 256;
+  const int smem = kStages2 * kStageBytes2 + 1024 + 256 + 4 * 2 * 2048;
   if ((e = ensure_smem_attr((const void*)kern, smem)) != cudaSuccess) return e;
   const int ntiles = p.tiles_w * p.tiles_x;
   const int maxpairs = num_sms_current() / 2;
@@ -933,7 +1092,7 @@ cudaError_t launch_tc2(TcParams p, const void* W, const void* X, int a_fmt, cuda
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if ((e = cudaLaunchKernelEx(&cfg, kern, p, mw, mx, mxh)) != cudaSuccess || p.splits == 1) return e;
+  if ((e = cudaLaunchKernelEx(&cfg, kern, p, mw, mx, mxh, md)) != cudaSuccess || p.splits == 1) return e;
   const dim3 rgrid((p.M + 31) / 32, (p.N + 31) / 32);
   tc_splitk_reduce_kernel<KIND><<<rgrid, dim3(32, 8), 0, stream>>>(p);
   return cudaGetLastError();
@@ -1163,3 +1322,9 @@ cudaError_t launch_gemm_tc_wgt(const void* A_f16, const uint8_t* B, float scale_
 }
 
 }  // namespace fp8imma_b200
+
+#ifdef FP8IMMA_TRACE
+extern "C" void fp8imma_debug_set_tc_trace(void* buf) {
+  fp8imma_b200::g_tc_trace = static_cast<unsigned long long*>(buf);
+}
+#endif

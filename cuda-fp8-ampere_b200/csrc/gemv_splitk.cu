@@ -449,7 +449,8 @@ __device__ __forceinline__ void peer_signal_and_wait(const GemvParams& p, unsign
       unsigned int v;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
       if ((int)(v - target) >= 0) break;
-      if (globaltimer_ns() - t0 > g_fp8imma_wait_limit_ns) {
+      const unsigned long long dt = globaltimer_ns() - t0;
+      if (dt > kWaitCheckNs && dt > *(volatile unsigned long long*)&g_fp8imma_wait_limit_ns) {
         atomicCAS(&g_fp8imma_device_error, 0u, ERR_WAIT_PEER);
         break;
       }
@@ -1031,9 +1032,10 @@ cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaSt
   const long long tiles = (p.N + kTileN - 1) / kTileN;
   if (!p.no_alloc && (fmt == FMT_E4M3_REF || fmt == FMT_E5M2) && (a_type == A_F16 || a_type == A_BF16) &&
       p.M >= 16 && (long long)p.M * p.K * tiles >= (16LL << 20) && p.keff_a == p.K) {
-    void* aq = nullptr;
-    cudaError_t e = cudaMallocAsync(&aq, (size_t)p.M * p.K, stream);
+    ScopedScratch sc;
+    cudaError_t e = sc.get((size_t)p.M * p.K, stream, kScratchGemvRows);
     if (e != cudaSuccess) return e;
+    void* aq = sc.ptr;
     e = launch_quant_a_s8(p.A, a_type, p.M, p.K, p.a_inv_h, p.row_inv_h, static_cast<int8_t*>(aq), stream);
     if (e == cudaSuccess) {
       GemvParams q = p;
@@ -1041,7 +1043,7 @@ cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaSt
       q.pdl = 1;  // weights stream while the pre-pass finishes; activations are read after it
       e = launch_gemv_impl(q, A_S8, fmt, splits, stream);
     }
-    cudaError_t e2 = cudaFreeAsync(aq, stream);
+    cudaError_t e2 = sc.release(stream);
     return e != cudaSuccess ? e : e2;
   }
   return launch_gemv_impl(p, a_type, fmt, splits, stream);

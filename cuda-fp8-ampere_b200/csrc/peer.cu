@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(kGatherThreads) peer_gather_kernel(const __gri
       if ((int)(v - target) >= 0) break;
       unsigned long long now;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-      if (now - t0 > g_peer_wait_ns) {
+      if (now - t0 > 1000000ull && now - t0 > *(volatile unsigned long long*)&g_peer_wait_ns) {  // read only after 1 ms
         atomicCAS(&g_peer_error, 0u, 5u);
         break;
       }

@@ -25,6 +25,7 @@ enum : unsigned int {
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any healthy wait
+constexpr unsigned long long kWaitCheckNs = 1000000ull;     // 1 ms: waits shorter than this never read the limit
 
 // The limit the waits use; kWaitLimitNs unless the host changed it
 // (fp8imma_set_wait_limit_ns). One per translation unit and device, like the
@@ -98,10 +99,12 @@ template <bool kSuspend = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int err_code) {
   if (mbar_try_wait<kSuspend>(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
-  const unsigned long long limit = *(volatile unsigned long long*)&g_fp8imma_wait_limit_ns;
   for (unsigned int i = 1;; ++i) {
     if (mbar_try_wait<kSuspend>(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > limit) break;
+    const unsigned long long dt = globaltimer_ns() - t0;
+    // the limit (a global load) is read only once a wait has lasted 1 ms,
+    // which no healthy wait does: limits below 1 ms act as 1 ms
+    if (dt > kWaitCheckNs && dt > *(volatile unsigned long long*)&g_fp8imma_wait_limit_ns) break;
   }
   atomicCAS(&g_fp8imma_device_error, 0u, err_code);
   return false;

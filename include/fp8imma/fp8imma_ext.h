@@ -200,7 +200,7 @@ const char* fp8imma_version(void);
 unsigned int fp8imma_device_error(int clear);
 // Wall-time limit of every bounded wait in the kernels (mbarrier pipelines,
 // the NVLink gather's peer flags) on the current device, in nanoseconds;
-// default 2e9. A wait that runs out records a code in the error word above and
+// default 2e9; values below 1e6 act as 1e6. A wait that runs out records a code in the error word above and
 // lets its kernel finish. No reference counterpart (failure handling).
 int fp8imma_set_wait_limit_ns(unsigned long long ns);
 
