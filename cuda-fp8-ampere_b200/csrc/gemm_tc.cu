@@ -146,6 +146,58 @@ struct TcParams {
   unsigned long long* trace;  // trace builds only: 64 words per CTA
 };
 
+// Epilogue of 32 accumulators (rows mbase .. mbase + 31 of weight column n):
+// scale, optional bias and activation, round to fp16 / bf16 and pack pairs.
+// Every decision (row scales, column scale, bias, activation, output type)
+// is uniform over the kernel, so each is taken once per 32 values rather
+// than per value: per-value branches, with the activations' tanhf / expf
+// inlined 32 times, made this loop cost more than the matrix product.
+// Arithmetic per value is unchanged: se = (cs * g) * cs2, v = acc * se
+// (int8 path) or v = (acc * g) * cs2 (fp32 path); v + bias rounded; act.
+template <int KIND>
+__device__ __forceinline__ void tc_epi_pack(const uint32_t (&r)[32], int mbase, float cs, float cs2, const TcParams& p,
+                                            int nb, uint32_t (&pk)[16]) {
+  float v[32];
+  const float c2 = p.col_scale_f32 ? cs2 : 1.0f;
+  if (p.row_g) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int m = mbase + j;
+      const float g = p.row_g[m < p.M ? m : 0];
+      if (KIND == KIND_I8)
+        v[j] = (float)(int32_t)r[j] * ((cs * g) * c2);
+      else
+        v[j] = __uint_as_float(r[j]) * g * cs2;
+    }
+  } else {
+    const float se = (cs * p.global_scale) * c2;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = KIND == KIND_I8 ? (float)(int32_t)r[j] * se : __uint_as_float(r[j]) * cs2;
+  }
+  if (p.bias) {
+    const float b = p.bias[nb];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], b);
+  }
+  if (p.act == 1) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = bias_act(v[j], nullptr, 0, 1);
+  } else if (p.act == 2) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = bias_act(v[j], nullptr, 0, 2);
+  } else if (p.act == 3) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = bias_act(v[j], nullptr, 0, 3);
+  }
+  if (p.out_bf16) {
+#pragma unroll
+    for (int w = 0; w < 16; ++w) pk[w] = (uint32_t)store_val(v[2 * w], 1) | ((uint32_t)store_val(v[2 * w + 1], 1) << 16);
+  } else {
+#pragma unroll
+    for (int w = 0; w < 16; ++w) pk[w] = (uint32_t)store_val(v[2 * w], 0) | ((uint32_t)store_val(v[2 * w + 1], 0) << 16);
+  }
+}
+
 template <int KIND>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     gemm_tc_kernel(const __grid_constant__ TcParams p, const __grid_constant__ CUtensorMap mapW,
@@ -274,21 +326,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         tmem_ld32(taddr + j0, r);
         const int mbase = tx * kTileX + j0;
         if (!nok || mbase >= p.M) continue;
+        uint32_t pk[16];
+        tc_epi_pack<KIND>(r, mbase, cs, cs2, p, n, pk);
         uint16_t o[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int m = mbase + j;
-          float v;
-          if (KIND == KIND_I8) {
-            float se = cs * (p.row_g ? p.row_g[m < p.M ? m : 0] : p.global_scale);
-            if (p.col_scale_f32) se = se * cs2;
-            v = (float)(int32_t)r[j] * se;
-          } else {
-            float rs = p.row_g ? p.row_g[m < p.M ? m : 0] : 1.0f;
-            v = __uint_as_float(r[j]) * rs * cs2;
-          }
-          o[j] = store_val(bias_act(v, p.bias, n, p.act), p.out_bf16);
-        }
+        for (int j = 0; j < 32; ++j) o[j] = (uint16_t)(pk[j >> 1] >> (16 * (j & 1)));
         const int mcount = min(32, p.M - mbase);
 #ifdef FP8IMMA_TC_EPI_DBG
         if (FP8IMMA_TC_EPI_DBG == 1) {
@@ -796,28 +838,18 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");  // this buffer's last store read it
           __syncwarp();
           uint32_t pk[16];
-#pragma unroll
-          for (int w2 = 0; w2 < 16; ++w2) {
-            const int m = mbase + 2 * w2;
-            float v0, v1;
-            if (KIND == KIND_I8) {
-              float se0 = cs * (p.row_g ? p.row_g[m < p.M ? m : 0] : p.global_scale);
-              float se1 = cs * (p.row_g ? p.row_g[m + 1 < p.M ? m + 1 : 0] : p.global_scale);
-              if (p.col_scale_f32) {
-                se0 = se0 * cs2;
-                se1 = se1 * cs2;
-              }
-              v0 = (float)(int32_t)r[2 * w2] * se0;
-              v1 = (float)(int32_t)r[2 * w2 + 1] * se1;
-            } else {
-              const float rs0 = p.row_g ? p.row_g[m < p.M ? m : 0] : 1.0f;
-              const float rs1 = p.row_g ? p.row_g[m + 1 < p.M ? m + 1 : 0] : 1.0f;
-              v0 = __uint_as_float(r[2 * w2]) * rs0 * cs2;
-              v1 = __uint_as_float(r[2 * w2 + 1]) * rs1 * cs2;
-            }
-            pk[w2] = (uint32_t)store_val(bias_act(v0, p.bias, nok ? n : 0, p.act), p.out_bf16) |
-                     ((uint32_t)store_val(bias_act(v1, p.bias, nok ? n : 0, p.act), p.out_bf16) << 16);
+          tc_epi_pack<KIND>(r, mbase, cs, cs2, p, nok ? n : 0, pk);
+#if defined(FP8IMMA_TC_EPI_DBG) && FP8IMMA_TC_EPI_DBG == 5
+          _Pragma("unroll") for (int w2 = 0; w2 < 16; ++w2) pk[w2] = (r[2 * w2] & 0xFFFFu) | (r[2 * w2 + 1] << 16);
+#endif
+#if defined(FP8IMMA_TC_EPI_DBG) && FP8IMMA_TC_EPI_DBG == 6
+          {
+            uint32_t x = 0;
+            _Pragma("unroll") for (int w2 = 0; w2 < 16; ++w2) x ^= pk[w2] * (w2 + 1);
+            if (x == 0x12345679u) D[0] = 1;
+            continue;
           }
+#endif
           uint4* row4 = reinterpret_cast<uint4*>(st + lane * 16);
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) row4[v4] = make_uint4(pk[4 * v4], pk[4 * v4 + 1], pk[4 * v4 + 2], pk[4 * v4 + 3]);
@@ -863,21 +895,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           _Pragma("unroll") for (int j = 0; j < 32; ++j) if (j < mc) C[(size_t)(mbase + j) * p.N + n] = __uint_as_float(r[j]);
           continue;
         }
+        uint32_t pk[16];
+        tc_epi_pack<KIND>(r, mbase, cs, cs2, p, n, pk);
         uint16_t o[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int m = mbase + j;
-          float v;
-          if (KIND == KIND_I8) {
-            float se = cs * (p.row_g ? p.row_g[m < p.M ? m : 0] : p.global_scale);
-            if (p.col_scale_f32) se = se * cs2;
-            v = (float)(int32_t)r[j] * se;
-          } else {
-            float rs = p.row_g ? p.row_g[m < p.M ? m : 0] : 1.0f;
-            v = __uint_as_float(r[j]) * rs * cs2;
-          }
-          o[j] = store_val(bias_act(v, p.bias, n, p.act), p.out_bf16);
-        }
+        for (int j = 0; j < 32; ++j) o[j] = (uint16_t)(pk[j >> 1] >> (16 * (j & 1)));
         const int mcount = min(32, p.M - mbase);
 #ifdef FP8IMMA_TC_EPI_DBG
         if (FP8IMMA_TC_EPI_DBG == 1) {
