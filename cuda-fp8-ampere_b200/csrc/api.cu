@@ -449,7 +449,7 @@ int fp8imma_set_tc_pair(int enable) {
 }
 
 int fp8imma_set_decode_kernel(int enable) {
-  if (enable != 0 && enable != 1) return (int)cudaErrorInvalidValue;
+  if (enable < 0 || enable > 2) return (int)cudaErrorInvalidValue;
   decode_set_mode(enable);
   return 0;
 }

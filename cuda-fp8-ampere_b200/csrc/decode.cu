@@ -68,6 +68,7 @@ struct DecodeCfg {
   int astride;      // int8 activation row stride in shared memory (kper + 64)
   int stage_bytes;  // gmax * 1024
   int arows;        // activation rows moved per box (min(M, 16))
+  int pre;          // the ring holds the whole K-slice: weights transcoded before the activations arrive
   int off_bar, off_const, off_raw, off_aq, off_tot, off_recv;
 };
 
@@ -99,6 +100,10 @@ __device__ __forceinline__ uint4 dec_lds128(uint32_t addr) {
   uint4 r;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr));
   return r;
+}
+
+__device__ __forceinline__ void dec_sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
 }
 
 __device__ __forceinline__ uint16_t dec_scale_bits(const GemvParams& p, int n) {
@@ -220,13 +225,13 @@ __device__ __forceinline__ void dec_store(const GemvParams& p, int n, int m, int
 // transcodes, four MMAs into four accumulator sets.
 // Activation fragment layout: `a_half` bytes from K half 0 to half 1 of a
 // stage, `a_hi` bytes from rows 0..7 to rows 8..15.
-template <int FMT, bool FAST>
+template <int FMT, bool FAST, bool PRE>
 __device__ __forceinline__ void dec_stage(int (&acc)[2][2][4], uint32_t w_addr, uint32_t a_addr, int a_half, int a_hi,
                                           bool hi_rows, uint32_t fs, uint16_t inv, int sw0, int sw1, int dbg) {
   const uint4 w0 = dec_lds128(w_addr + sw0);
   const uint4 w1 = dec_lds128(w_addr + sw1);
   uint32_t b[2][4];
-  if (DEC_DBG(4)) {  // experiment: no transcode
+  if (PRE || DEC_DBG(4)) {  // weights transcoded ahead (or experiment: no transcode)
     b[0][0] = w0.x; b[0][1] = w0.y; b[0][2] = w0.z; b[0][3] = w0.w;
     b[1][0] = w1.x; b[1][1] = w1.y; b[1][2] = w1.z; b[1][3] = w1.w;
   } else {
@@ -256,13 +261,19 @@ __device__ __forceinline__ void dec_stage(int (&acc)[2][2][4], uint32_t w_addr, 
 // Two stages of a consumer warp at once: sixteen independent transcodes in
 // flight (the warp count per SM is low, so the latency is hidden inside the
 // warp), their MMAs into a second set of accumulators.
-template <int FMT, bool FAST>
+template <int FMT, bool FAST, bool PRE>
 __device__ __forceinline__ void dec_stage2(int (&accA)[2][2][4], int (&accB)[2][2][4], uint32_t wA, uint32_t wB,
                                            uint32_t aA, uint32_t aB, int a_half, int a_hi, bool hi_rows, uint32_t fs,
                                            uint16_t inv, int sw0, int sw1) {
   const uint4 x0 = dec_lds128(wA + sw0), x1 = dec_lds128(wA + sw1);
   const uint4 y0 = dec_lds128(wB + sw0), y1 = dec_lds128(wB + sw1);
   uint32_t bA[2][4], bB[2][4];
+  if (PRE) {
+    bA[0][0] = x0.x; bA[0][1] = x0.y; bA[0][2] = x0.z; bA[0][3] = x0.w;
+    bA[1][0] = x1.x; bA[1][1] = x1.y; bA[1][2] = x1.z; bA[1][3] = x1.w;
+    bB[0][0] = y0.x; bB[0][1] = y0.y; bB[0][2] = y0.z; bB[0][3] = y0.w;
+    bB[1][0] = y1.x; bB[1][1] = y1.y; bB[1][2] = y1.z; bB[1][3] = y1.w;
+  } else {
   bA[0][0] = dec_tc4<FMT, FAST>(x0.x, fs, inv);
   bB[0][0] = dec_tc4<FMT, FAST>(y0.x, fs, inv);
   bA[0][1] = dec_tc4<FMT, FAST>(x0.y, fs, inv);
@@ -279,6 +290,7 @@ __device__ __forceinline__ void dec_stage2(int (&accA)[2][2][4], int (&accB)[2][
   bB[1][2] = dec_tc4<FMT, FAST>(y1.z, fs, inv);
   bA[1][3] = dec_tc4<FMT, FAST>(x1.w, fs, inv);
   bB[1][3] = dec_tc4<FMT, FAST>(y1.w, fs, inv);
+  }
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const uint4 u = dec_lds128(aA + a_half * h);
@@ -295,11 +307,76 @@ __device__ __forceinline__ void dec_stage2(int (&accA)[2][2][4], int (&accB)[2][
   }
 }
 
+// Weights ahead of the activations: when the ring holds the whole K-slice,
+// each consumer warp transcodes its stages (i = q mod W) in place, FP8 bytes
+// -> int8 bytes at the same shared memory addresses, as they land. This runs
+// while the activation rows are still to come (they follow the previous
+// kernel), so the ALU-bound transcode overlaps the call's head instead of
+// following it. Each lane rewrites exactly the 32 bytes it read, so no other
+// thread's data is touched.
+template <int FMT, bool FAST>
+__device__ __forceinline__ bool dec_pretranscode(uint32_t stages_a, uint64_t* full, int stage_bytes, int nst, int c,
+                                                 int q, int lane, uint32_t fs, uint16_t inv) {
+  constexpr int W = kDecWpg;
+  const int g = lane >> 2, t = lane & 3;
+  const int sg = (g >> 1) + 4 * (g & 1);
+  const uint32_t wrow = stages_a + (8 * c + sg) * kDecBoxK;
+  const int sw0 = (t ^ sg) << 4, sw1 = ((4 + t) ^ sg) << 4;
+  bool ok = true;
+  int i = q;
+  for (; i + W < nst; i += 2 * W) {
+    if (ok) ok = dec_wait(&full[i], 0, ERR_WAIT_FULL);
+    if (ok) ok = dec_wait(&full[i + W], 0, ERR_WAIT_FULL);
+    const uint32_t a = wrow + i * stage_bytes, b = wrow + (i + W) * stage_bytes;
+    const uint4 x0 = dec_lds128(a + sw0), x1 = dec_lds128(a + sw1);
+    const uint4 y0 = dec_lds128(b + sw0), y1 = dec_lds128(b + sw1);
+    uint4 u0, u1, v0, v1;
+    u0.x = dec_tc4<FMT, FAST>(x0.x, fs, inv);
+    v0.x = dec_tc4<FMT, FAST>(y0.x, fs, inv);
+    u0.y = dec_tc4<FMT, FAST>(x0.y, fs, inv);
+    v0.y = dec_tc4<FMT, FAST>(y0.y, fs, inv);
+    u0.z = dec_tc4<FMT, FAST>(x0.z, fs, inv);
+    v0.z = dec_tc4<FMT, FAST>(y0.z, fs, inv);
+    u0.w = dec_tc4<FMT, FAST>(x0.w, fs, inv);
+    v0.w = dec_tc4<FMT, FAST>(y0.w, fs, inv);
+    u1.x = dec_tc4<FMT, FAST>(x1.x, fs, inv);
+    v1.x = dec_tc4<FMT, FAST>(y1.x, fs, inv);
+    u1.y = dec_tc4<FMT, FAST>(x1.y, fs, inv);
+    v1.y = dec_tc4<FMT, FAST>(y1.y, fs, inv);
+    u1.z = dec_tc4<FMT, FAST>(x1.z, fs, inv);
+    v1.z = dec_tc4<FMT, FAST>(y1.z, fs, inv);
+    u1.w = dec_tc4<FMT, FAST>(x1.w, fs, inv);
+    v1.w = dec_tc4<FMT, FAST>(y1.w, fs, inv);
+    dec_sts128(a + sw0, u0);
+    dec_sts128(a + sw1, u1);
+    dec_sts128(b + sw0, v0);
+    dec_sts128(b + sw1, v1);
+  }
+  for (; i < nst; i += W) {
+    if (ok) ok = dec_wait(&full[i], 0, ERR_WAIT_FULL);
+    const uint32_t a = wrow + i * stage_bytes;
+    const uint4 x0 = dec_lds128(a + sw0), x1 = dec_lds128(a + sw1);
+    uint4 u0, u1;
+    u0.x = dec_tc4<FMT, FAST>(x0.x, fs, inv);
+    u0.y = dec_tc4<FMT, FAST>(x0.y, fs, inv);
+    u0.z = dec_tc4<FMT, FAST>(x0.z, fs, inv);
+    u0.w = dec_tc4<FMT, FAST>(x0.w, fs, inv);
+    u1.x = dec_tc4<FMT, FAST>(x1.x, fs, inv);
+    u1.y = dec_tc4<FMT, FAST>(x1.y, fs, inv);
+    u1.z = dec_tc4<FMT, FAST>(x1.z, fs, inv);
+    u1.w = dec_tc4<FMT, FAST>(x1.w, fs, inv);
+    dec_sts128(a + sw0, u0);
+    dec_sts128(a + sw1, u1);
+  }
+  __syncwarp();  // the warp's later fragment loads see every lane's int8 bytes
+  return ok;
+}
+
 // Activation layouts: quantised in the kernel (direct = false: row stride
 // astride, K contiguous) or copied by TMA as int8 boxes of 16 rows x 64 bytes
 // (direct = true: box j = K bytes [64j, 64j + 64) at j * 1024, rows 64 bytes
 // apart, so each 8-lane phase of a fragment load covers all 32 banks).
-template <int FMT, bool FAST, int W>
+template <int FMT, bool FAST, int W, bool PRE>
 __device__ __forceinline__ bool dec_loop(int (&acc)[2][2][4], uint32_t stages_a, uint64_t* full, uint64_t* empty,
                                          uint32_t aq_a, bool direct, int astride, int stage_bytes, int D, int nst,
                                          int c, int q, int lane, bool hi_rows, uint32_t fs, uint16_t inv, int dbg) {
@@ -335,9 +412,9 @@ __device__ __forceinline__ bool dec_loop(int (&acc)[2][2][4], uint32_t stages_a,
     int s2 = s;
     uint32_t phase2 = phase;
     advance(s2, phase2);
-    if (ok && !DEC_DBG(1)) ok = dec_wait(&full[s], phase, ERR_WAIT_FULL);
-    if (ok && !DEC_DBG(1)) ok = dec_wait(&full[s2], phase2, ERR_WAIT_FULL);
-    dec_stage2<FMT, FAST>(acc, acc2, wrow + s * stage_bytes, wrow + s2 * stage_bytes, a_addr, a_addr + W * a_stage,
+    if (!PRE && ok && !DEC_DBG(1)) ok = dec_wait(&full[s], phase, ERR_WAIT_FULL);
+    if (!PRE && ok && !DEC_DBG(1)) ok = dec_wait(&full[s2], phase2, ERR_WAIT_FULL);
+    dec_stage2<FMT, FAST, PRE>(acc, acc2, wrow + s * stage_bytes, wrow + s2 * stage_bytes, a_addr, a_addr + W * a_stage,
                           a_half, a_hi, hi_rows, fs, inv, sw0, sw1);
     if (recycle) {  // the producer refills these slots: release them once every lane has read them
       __syncwarp();
@@ -352,8 +429,8 @@ __device__ __forceinline__ bool dec_loop(int (&acc)[2][2][4], uint32_t stages_a,
     advance(s, phase);
   }
   for (; i < nst; i += W) {
-    if (ok && !DEC_DBG(1)) ok = dec_wait(&full[s], phase, ERR_WAIT_FULL);
-    dec_stage<FMT, FAST>(acc, wrow + s * stage_bytes, a_addr, a_half, a_hi, hi_rows, fs, inv, sw0, sw1, dbg);
+    if (!PRE && ok && !DEC_DBG(1)) ok = dec_wait(&full[s], phase, ERR_WAIT_FULL);
+    dec_stage<FMT, FAST, PRE>(acc, wrow + s * stage_bytes, a_addr, a_half, a_hi, hi_rows, fs, inv, sw0, sw1, dbg);
     if (recycle) {
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
@@ -422,7 +499,9 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
   // before the CTA-wide barrier: nothing waits on them before it.
   const CUtensorMap* tm = G == cfg.gmax ? &tm_full : &tm_short;
   const uint32_t wbytes = (uint32_t)G * 8 * kDecBoxK;
-  const int early = min(nst, min(cfg.D, kDecEarlyStages));
+  // with the whole K-slice resident every stage is requested at once (the
+  // consumers transcode them while the activation rows are still to come)
+  const int early = cfg.pre ? nst : min(nst, min(cfg.D, kDecEarlyStages));
   uint8_t* adst = kDirect ? reinterpret_cast<uint8_t*>(aq) : raw;
   const bool producer = warp == cwarps && lane == 0 && G > 0;
   DEC_TRACE(10);
@@ -490,6 +569,17 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
     const bool col_ok = active && col < p.N;
     const uint16_t sb = col_ok ? dec_scale_bits(p, col) : (uint16_t)0;
     const int tid = threadIdx.x;
+    const uint16_t inv = col_ok ? inv_scale_bits(sb) : (uint16_t)0x3C00u;
+    const bool all_fast = named_bar_and(2, nthr, fast_ok<FMT>(inv));  // CTA-uniform transcode choice
+    const uint32_t fs = fast_scale<FMT>(inv);
+    bool pre_ok = true;
+    if (cfg.pre && active) {
+      if (all_fast)
+        pre_ok = dec_pretranscode<FMT, true>(smem_u32(stages), full, cfg.stage_bytes, nst, c, q, lane, fs, inv);
+      else
+        pre_ok = dec_pretranscode<FMT, false>(smem_u32(stages), full, cfg.stage_bytes, nst, c, q, lane, fs, inv);
+    }
+    DEC_TRACE(12);
     float scv = 0.0f, csv = 1.0f;
     if (tid < 8 * G && n0 + tid < p.N) {
       scv = __half2float(__ushort_as_half(dec_scale_bits(p, n0 + tid)));
@@ -505,17 +595,16 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
       rg_s[tid] = live ? (p.row_g ? p.row_g[tid] : p.global_scale) : 0.0f;
       rowinv_s[tid] = (live && p.row_inv_h) ? p.row_inv_h[tid] : p.a_inv_h;
     }
-    const uint16_t inv = col_ok ? inv_scale_bits(sb) : (uint16_t)0x3C00u;
-    named_bar_sync(1, nthr);  // rowinv_s
+    if (!kDirect) named_bar_sync(1, nthr);  // rowinv_s
     DEC_TRACE(3);
     if (nbox > 0) dec_wait(act_bar, 0, ERR_WAIT_FULL);
     DEC_TRACE(9);
-    if (!kDirect) dec_quant_rows<AT>(raw, aq, cfg.astride, nbox, cfg.arows, rowinv_s, tid, nthr);
-    // CTA-uniform transcode choice; also the barrier that publishes the int8 rows
-    const bool all_fast = named_bar_and(2, nthr, fast_ok<FMT>(inv));
+    if (!kDirect) {
+      dec_quant_rows<AT>(raw, aq, cfg.astride, nbox, cfg.arows, rowinv_s, tid, nthr);
+      named_bar_sync(1, nthr);  // publishes the int8 rows
+    }
     DEC_TRACE(4);
-    const uint32_t fs = fast_scale<FMT>(inv);
-    if (active) {
+    if (active && pre_ok) {
       const uint32_t st_a = smem_u32(stages), aq_a = smem_u32(aq);
       const bool hi_rows = p.M > 8;  // rows 8..15 of the m16 block hold data
 #ifdef FP8IMMA_TRACE
@@ -523,12 +612,15 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
 #else
       const int dbg = 0;
 #endif
-      if (all_fast)
-        dec_loop<FMT, true, kDecWpg>(acc, st_a, full, empty, aq_a, kDirect, cfg.astride, cfg.stage_bytes, cfg.D, nst,
-                                     c, q, lane, hi_rows, fs, inv, dbg);
+      if (cfg.pre)
+        dec_loop<FMT, true, kDecWpg, true>(acc, st_a, full, empty, aq_a, kDirect, cfg.astride, cfg.stage_bytes, cfg.D,
+                                           nst, c, q, lane, hi_rows, fs, inv, dbg);
+      else if (all_fast)
+        dec_loop<FMT, true, kDecWpg, false>(acc, st_a, full, empty, aq_a, kDirect, cfg.astride, cfg.stage_bytes, cfg.D,
+                                            nst, c, q, lane, hi_rows, fs, inv, dbg);
       else
-        dec_loop<FMT, false, kDecWpg>(acc, st_a, full, empty, aq_a, kDirect, cfg.astride, cfg.stage_bytes, cfg.D, nst,
-                                      c, q, lane, hi_rows, fs, inv, dbg);
+        dec_loop<FMT, false, kDecWpg, false>(acc, st_a, full, empty, aq_a, kDirect, cfg.astride, cfg.stage_bytes,
+                                             cfg.D, nst, c, q, lane, hi_rows, fs, inv, dbg);
     }
     DEC_TRACE(5);
   }
@@ -773,6 +865,7 @@ static bool decode_plan(int M, int N, int K, int a_bytes, int sms, DecodeCfg* ou
   D -= D % kDecWpg;  // a multiple of the warps per group: warp q keeps ring slots s = q (mod kDecWpg)
   if (D < kDecWpg) D = kDecWpg;
   cfg.D = D;
+  cfg.pre = nst <= D && g_decode_mode.load() != 2;
   size_t off = (size_t)D * cfg.stage_bytes;
   cfg.off_raw = (int)off;  // 1024-aligned (stages are multiples of 1 KB)
   off += raw;

@@ -179,8 +179,11 @@ int fp8imma_set_tc_tile_x(int rows);
 int fp8imma_set_tc_half_tail(int enable);
 // 1 (default): small-M shapes that fit one wave of at most 64 weight columns
 // per SM (e.g. N = K = 4096) run the balanced decode kernel (one CTA per SM,
-// CTA pairs splitting K); 0: they run the split-K cluster kernel. Results are
-// identical either way. No reference counterpart (tuning switch).
+// CTA pairs splitting K); 2: the decode kernel without the early weight
+// transcode (it otherwise converts its weights to int8 in shared memory while
+// the activations are still to come); 0: they run the split-K cluster kernel.
+// Results are identical in every mode. No reference counterpart (tuning
+// switch).
 int fp8imma_set_decode_kernel(int enable);
 // Programmatic dependent launch (default on). A small-M GEMM then starts
 // streaming its weights and reading its column scales while the previous
