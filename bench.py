@@ -58,6 +58,17 @@ def alg_bytes(M, N, K):
     return N * K + 4 * N + 2 * M * K + 2 * M * N
 
 
+def sustained_bf16():
+    """MEASURED_PEAKS.json's sustained (power-capped) bf16 TFLOP/s, else the
+    earlier measurement on this pool (1.4 PFLOP/s)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        if "bf16_tflops_sustained" in d:
+            return float(d["bf16_tflops_sustained"])
+    return 1400.0
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -603,10 +614,16 @@ def time_metric_points(ext, gpu_index, hbm, bf16, peak_kind):
         ms, clocks = _timed_graph(call, n_calls, gpu_index, min_ms)
         path = ext.last_path()
         if M > 64:
+            # timed for >= 50 ms back to back: the power-capped (sustained)
+            # regime, so the sustained peak is the denominator; the burst
+            # fraction is reported beside it
             achieved = 2.0 * M * N * K / (ms * 1e-3) / 1e12
-            roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": 2.0 * bf16, "unit": "TFLOP/s",
-                    "frac": round(achieved / (2.0 * bf16), 4),
-                    "peak_source": "2 x MEASURED_PEAKS.json bf16_tflops (%s)" % peak_kind}
+            sus = sustained_bf16()
+            roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(2.0 * sus, 1),
+                    "unit": "TFLOP/s", "frac": round(achieved / (2.0 * sus), 4),
+                    "frac_of_burst": round(achieved / (2.0 * bf16), 4),
+                    "peak_source": "2 x MEASURED_PEAKS.json bf16_tflops_sustained (%s); int8 dense = 2x bf16 nominal"
+                                   % peak_kind}
             val, unit = achieved, "TFLOPS"
         else:
             achieved = alg_bytes(M, N, K) / (ms * 1e-3) / 1e9

@@ -102,6 +102,7 @@ struct TcParams {
   int kb_per_split;    // 128-byte K blocks per split
   uint32_t* ws;        // splits > 1: raw accumulators [split][n][m] (int32 or fp32 bits)
   int tma_out;         // CTA-pair kernel: col-major 16-bit output written by TMA stores (mapD)
+  int pdl;             // CTA-pair kernel launched as a programmatic dependent of the prep kernels
   unsigned long long* trace;  // trace builds only: 64 words per CTA
 };
 
@@ -339,9 +340,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 // multiplier), 8 elements per thread-iteration. K % 8 == 0.
 template <int AT>
 __global__ void __launch_bounds__(256) quant_a_s8_kernel(const void* __restrict__ A, int M, int K, uint16_t a_inv_h,
-                                                         const uint16_t* __restrict__ row_inv_h, int8_t* __restrict__ Aq) {
+                                                         const uint16_t* __restrict__ row_inv_h, int8_t* __restrict__ Aq,
+                                                         int after_prev) {
   // the GEMM that consumes these rows may be launched as a programmatic
-  // dependent: it starts streaming its weights now and waits for this grid
+  // dependent: it sets itself up now and waits for this grid
   // (griddepcontrol.wait) before it reads the quantised rows
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const size_t total = (size_t)M * (K >> 3);
@@ -366,6 +368,10 @@ __global__ void __launch_bounds__(256) quant_a_s8_kernel(const void* __restrict_
     }
     reinterpret_cast<uint2*>(Aq)[i] = out;
   }
+  // launched as a programmatic dependent of the weight transcode (which it
+  // overlaps): finish only after that grid, so that a kernel waiting for this
+  // one also waits for the transcode
+  if (after_prev) asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // FP8 weights -> int8 with the reference chain. One warp per weight row at a
@@ -376,6 +382,7 @@ template <int FMT>
 __global__ void __launch_bounds__(256) transcode_b_kernel(const uint8_t* __restrict__ B, int N, int K,
                                                           const uint16_t* __restrict__ scale_u16,
                                                           unsigned long long scale_tex, int8_t* __restrict__ Bq) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the activation quantisation may run alongside
   const int lane = threadIdx.x & 31;
   const int warps = gridDim.x * (blockDim.x >> 5);
   const int k16 = K >> 4;  // 16-byte vectors per row
@@ -671,6 +678,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       prefetch_tensormap(&mapW);
       prefetch_tensormap(&mapX);
       prefetch_tensormap(&mapXh);
+      // as a programmatic dependent the CTA set itself up beside the prep
+      // kernels; their operands are read only after they have finished
+      if (p.pdl) pdl_wait();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -1066,13 +1076,18 @@ cudaError_t launch_tc2(TcParams p, const void* W, const void* X, int a_fmt, cuda
   cfg.blockDim = dim3(kThreadsTC, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  // (not with K splits: the finishing pass follows, and mid-M calls measured
+  // slower as programmatic dependents, 44 vs 37 us at M = 128, N = K = 4096)
+  if (p.splits > 1) p.pdl = 0;
+  cfg.numAttrs = p.pdl ? 2 : 1;
   if ((e = cudaLaunchKernelEx(&cfg, kern, p, mw, mx, mxh, md)) != cudaSuccess || p.splits == 1) return e;
   const dim3 rgrid((p.M + 31) / 32, (p.N + 31) / 32);
   tc_splitk_reduce_kernel<KIND><<<rgrid, dim3(32, 8), 0, stream>>>(p);
@@ -1146,17 +1161,10 @@ cudaError_t launch_gemm_tc_s8(const GemvParams& gp, int a_type, int fmt, void* s
   const int M = gp.M, N = gp.N, K = gp.K;
   int8_t* Aq = static_cast<int8_t*>(scratch);
   int8_t* Bq = Aq + (((size_t)M * K + 255) & ~size_t(255));
-  // 1. activations
-  {
-    const size_t items = (size_t)M * (K >> 3);
-    const int grid = grid_for(items);
-    switch (a_type) {
-      case A_F16: quant_a_s8_kernel<A_F16><<<grid, 256, 0, stream>>>(gp.A, M, K, gp.a_inv_h, gp.row_inv_h, Aq); break;
-      case A_BF16: quant_a_s8_kernel<A_BF16><<<grid, 256, 0, stream>>>(gp.A, M, K, gp.a_inv_h, gp.row_inv_h, Aq); break;
-      default: quant_a_s8_kernel<A_S8><<<grid, 256, 0, stream>>>(gp.A, M, K, gp.a_inv_h, gp.row_inv_h, Aq); break;
-    }
-  }
-  // 2. weights: one warp per row, at most 8 resident CTAs of 8 warps per SM
+  const bool pdl = gp.pdl != 0;
+  // 1. weights: one warp per row, at most 8 resident CTAs of 8 warps per SM.
+  // An ordinary launch: it overwrites scratch that the previous call's GEMM
+  // on this stream may still read.
   {
     const int sms = num_sms_current();
     const int grid = std::min((N + 7) / 8, sms * 8);
@@ -1167,6 +1175,34 @@ cudaError_t launch_gemm_tc_s8(const GemvParams& gp, int a_type, int fmt, void* s
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  // 2. activations, alongside the transcode when programmatic dependent
+  // launch is on (the two touch disjoint memory; everything before the call
+  // has finished once the transcode started)
+  {
+    const size_t items = (size_t)M * (K >> 3);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)grid_for(items), 1, 1);
+    lc.blockDim = dim3(256, 1, 1);
+    lc.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = pdl ? 1 : 0;
+    const int after = pdl ? 1 : 0;
+    switch (a_type) {
+      case A_F16:
+        e = cudaLaunchKernelEx(&lc, quant_a_s8_kernel<A_F16>, gp.A, M, K, gp.a_inv_h, gp.row_inv_h, Aq, after);
+        break;
+      case A_BF16:
+        e = cudaLaunchKernelEx(&lc, quant_a_s8_kernel<A_BF16>, gp.A, M, K, gp.a_inv_h, gp.row_inv_h, Aq, after);
+        break;
+      default:
+        e = cudaLaunchKernelEx(&lc, quant_a_s8_kernel<A_S8>, gp.A, M, K, gp.a_inv_h, gp.row_inv_h, Aq, after);
+        break;
+    }
+    if (e != cudaSuccess) return e;
+  }
   // 3. tensor-core GEMM
   CUtensorMap mw, mx;
   if ((e = make_tmap_2d_u8(&mw, Bq, K, N, K, kBK, kTileW, true)) != cudaSuccess) return e;
@@ -1192,6 +1228,7 @@ cudaError_t launch_gemm_tc_s8(const GemvParams& gp, int a_type, int fmt, void* s
   if (g_use_pair) {
     p.splits = tc_pick_splits(M, N, K);
     p.ws = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(scratch) + tc_ws_offset(M, N, K, false));
+    p.pdl = pdl ? 1 : 0;
     return launch_tc2<KIND_I8>(p, Bq, Aq, 0, stream);
   }
   return launch_tc<KIND_I8>(p, mw, mx, stream);
@@ -1204,8 +1241,8 @@ cudaError_t launch_quant_a_s8(const void* A, int a_type, int M, int K, uint16_t 
                               int8_t* Aq, cudaStream_t stream) {
   const int grid = grid_for((size_t)M * (K >> 3));
   switch (a_type) {
-    case A_F16: quant_a_s8_kernel<A_F16><<<grid, 256, 0, stream>>>(A, M, K, a_inv_h, row_inv_h, Aq); break;
-    case A_BF16: quant_a_s8_kernel<A_BF16><<<grid, 256, 0, stream>>>(A, M, K, a_inv_h, row_inv_h, Aq); break;
+    case A_F16: quant_a_s8_kernel<A_F16><<<grid, 256, 0, stream>>>(A, M, K, a_inv_h, row_inv_h, Aq, 0); break;
+    case A_BF16: quant_a_s8_kernel<A_BF16><<<grid, 256, 0, stream>>>(A, M, K, a_inv_h, row_inv_h, Aq, 0); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

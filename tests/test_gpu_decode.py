@@ -26,9 +26,10 @@ DECODE_PATH = 6
 # shard (N = 3584, K = 8192; it fits only with the activation pre-pass of
 # M >= 8), K not a multiple of 128 or 64, N not a multiple of 8, fewer groups
 # than SMs, K = 128 (no pair: one CTA per cluster), M = 9..15 (rows 8..15
-# partly live)
+# partly live), 8 groups per CTA (the 17-warp instantiation: N = 9000, one CTA
+# per cluster)
 SHAPES = [(1, 4096, 4096), (16, 4096, 4096), (4, 4096, 4096), (16, 3584, 8192), (3, 200, 528), (9, 1003, 1040),
-          (16, 8, 256), (2, 24, 4160), (12, 7168, 1024), (8, 513, 128), (15, 1200, 2112)]
+          (16, 8, 256), (2, 24, 4160), (12, 7168, 1024), (8, 513, 128), (15, 1200, 2112), (4, 9000, 1024)]
 
 
 @pytest.fixture
