@@ -419,7 +419,7 @@ def main():
     # one GPU: the K steps (copy in, GEMM, copy out each) captured in a CUDA
     # graph like the kernel timing, so host launch overhead is not the clock
     e2e_graph, e2e_timing = None, "eager launches"
-    if world == 1:
+    if world == 1 or fused is not None:  # (the NVLink gather counts its calls on the device: replayable)
         try:
             e2e_graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(e2e_graph, stream=stream):
@@ -430,10 +430,12 @@ def main():
             e2e_graph.replay()
             torch.cuda.synchronize()
             e2e_timing = ("CUDA graph of K steps (H2D copy, GEMM, D2H copy per step; consecutive steps on two "
-                          "streams, so one step's copies overlap the other's GEMM)")
+                          "streams, so one step's copies overlap the other's GEMM)") if world == 1 else (
+                              "CUDA graph of K steps (H2D copy, GEMM, NVLink gather, D2H copy per step)")
         except Exception:
             e2e_graph = None
             torch.cuda.synchronize()
+    barrier()
     with torch.cuda.stream(stream):
         ev0.record()
         if e2e_graph is not None:

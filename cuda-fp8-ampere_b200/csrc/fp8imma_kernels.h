@@ -149,9 +149,10 @@ cudaError_t launch_quant_a_e4m3(const void* A, int a_type, int M, int K, uint8_t
 
 // Push this rank's rows [row0, row0+rows) of a [*, M] fp16 buffer into every
 // peer's buffer at the same rows, then wait until every peer has done the
-// same (bounded wait; a timeout records a code and returns).
+// same (bounded wait; a timeout records a code and returns). pdl: launched as
+// a programmatic dependent of the GEMM that wrote the rows.
 cudaError_t launch_peer_gather(const unsigned long long* outs, const unsigned long long* pads, int world, int rank,
-                               size_t row0, size_t rows, int M, unsigned int epoch, cudaStream_t stream);
+                               size_t row0, size_t rows, int M, unsigned int epoch, bool pdl, cudaStream_t stream);
 unsigned int peer_device_error(bool clear);
 
 // Exact fallback for shapes the fast kernels do not take (any K, any alignment).

@@ -35,6 +35,11 @@ __global__ void __launch_bounds__(kGatherThreads) peer_gather_kernel(const __gri
                                                                      const __grid_constant__ Ptrs8 pads, int world, int rank,
                                                                      unsigned long long byte0, unsigned long long nbytes,
                                                                      unsigned int epoch_arg) {
+  // launched as a programmatic dependent of the GEMM: the next call's kernels
+  // may start (they wait for this grid before touching its buffers), and this
+  // grid waits for the GEMM's rows before copying them
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // 1. copy this rank's rows to every peer (grid-strided). byte0 = rank * N *
   //    M * 2 is only as aligned as N * M allows, so 16-byte granules are used
   //    only when both addresses are 16-byte aligned (all ranks' buffers share
@@ -103,15 +108,23 @@ __global__ void __launch_bounds__(kGatherThreads) peer_gather_kernel(const __gri
 }  // namespace
 
 cudaError_t launch_peer_gather(const unsigned long long* outs, const unsigned long long* pads, int world, int rank,
-                               size_t row0, size_t rows, int M, unsigned int epoch, cudaStream_t stream) {
+                               size_t row0, size_t rows, int M, unsigned int epoch, bool pdl, cudaStream_t stream) {
   Ptrs8 o = {}, s = {};
   for (int i = 0; i < world; ++i) {
     o.p[i] = outs[i];
     s.p[i] = pads[i];
   }
-  peer_gather_kernel<<<kGatherBlocks, kGatherThreads, 0, stream>>>(o, s, world, rank, row0 * M * 2, rows * M * 2,
-                                                                   epoch);
-  return cudaGetLastError();
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(kGatherBlocks, 1, 1);
+  lc.blockDim = dim3(kGatherThreads, 1, 1);
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&lc, peer_gather_kernel, o, s, world, rank, (unsigned long long)(row0 * M * 2),
+                            (unsigned long long)(rows * M * 2), epoch);
 }
 
 cudaError_t peer_set_wait_limit(unsigned long long ns) { return cudaMemcpyToSymbol(g_peer_wait_ns, &ns, sizeof(ns)); }
@@ -169,6 +182,7 @@ extern "C" int fp8imma_gemm_allgather(const fp8imma_gemm_args* a, void* const* p
   p.global_scale = a->global_scale;
   p.a_inv_h = __half_as_ushort(__float2half(a->a_inv_scale));
   p.out_bf16 = a->out_type;
+  p.pdl = api_pdl();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (world > 1 && g_fused_gather) {
     // the split-K kernel's epilogue writes into every peer's output and
@@ -185,5 +199,6 @@ extern "C" int fp8imma_gemm_allgather(const fp8imma_gemm_args* a, void* const* p
   cudaError_t e = launch_gemv_s8(p, a->a_type, a->b_format, 0, st);
   if (e != cudaSuccess) return (int)e;
   if (world == 1) return 0;
-  return (int)launch_peer_gather(outs, pads, world, rank, (size_t)rank * a->N, (size_t)a->N, a->M, epoch, st);
+  return (int)launch_peer_gather(outs, pads, world, rank, (size_t)rank * a->N, (size_t)a->N, a->M, epoch, p.pdl != 0,
+                                 st);
 }
