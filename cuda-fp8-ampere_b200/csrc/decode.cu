@@ -447,6 +447,78 @@ __device__ __forceinline__ bool dec_loop(int (&acc)[2][2][4], uint32_t stages_a,
   return ok;
 }
 
+// ---- column-parallel gather fused into the epilogue (world > 1, col-major)
+// Every call adds exactly kDecPeerUnits to each peer counter whatever the
+// grid (CTA i adds floor((i+1)U/n) - floor(iU/n)), the same per-call total
+// and the same signal-pad slots as the split-K kernel's fused gather, so the
+// two kernels may alternate between calls.
+constexpr unsigned int kDecPeerUnits = 1u << 20;
+
+// This CTA's finished columns [c0, c1) (a contiguous run of the col-major
+// slice, already stored locally) into every peer's output, then one
+// system-scope release increment per peer.
+__device__ __forceinline__ void dec_peer_publish(const GemvParams& p, int c0, int c1) {
+  __syncthreads();  // the CTA's local output stores are done
+  if (c0 < c1) {
+    const size_t b0 = (size_t)c0 * p.M * 2, nb = (size_t)(c1 - c0) * p.M * 2;
+    const uint8_t* src = static_cast<const uint8_t*>(p.D) + b0;
+    for (int q = 0; q < p.world; ++q) {
+      if (q == p.rank) continue;
+      uint8_t* dst = reinterpret_cast<uint8_t*>(p.peer_rows[q]) + b0;
+      if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | nb) & 15u) == 0) {
+        for (size_t i = threadIdx.x; i < (nb >> 4); i += blockDim.x)
+          reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+      } else {
+        for (size_t i = threadIdx.x; i < (nb >> 1); i += blockDim.x)
+          reinterpret_cast<uint16_t*>(dst)[i] = reinterpret_cast<const uint16_t*>(src)[i];
+      }
+    }
+  }
+  __syncthreads();  // (orders every thread's peer stores before the release below)
+  if ((int)threadIdx.x < p.world && (int)threadIdx.x != p.rank) {
+    const unsigned long long U = kDecPeerUnits, n = gridDim.x, i = blockIdx.x;
+    const unsigned int share = (unsigned int)(((i + 1) * U) / n - (i * U) / n);
+    unsigned int* slot = reinterpret_cast<unsigned int*>(p.peer_sig[threadIdx.x]) + kPeerFusedSlot + p.rank;
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(slot), "r"(share) : "memory");
+  }
+}
+
+// One CTA, launched as a programmatic dependent of the decode kernel: advance
+// this rank's call epoch and wait (bounded) until every peer has published
+// this call's rows; finish only after the decode grid, so that whatever
+// follows in the stream sees the whole gathered output.
+__global__ void __launch_bounds__(32) dec_peer_wait_kernel(const __grid_constant__ GemvParams p) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  __shared__ unsigned int target_s;
+  if (threadIdx.x == 0) {
+    unsigned int e = p.epoch;
+    if (e == 0) {  // counted on the device: advances on every launch, graph replays included
+      unsigned int* ctr = reinterpret_cast<unsigned int*>(p.peer_sig[p.rank]) + kPeerFusedEpochSlot;
+      e = *ctr + 1;
+      *ctr = e;
+    }
+    target_s = e * kDecPeerUnits;  // modulo 2^32; compared by signed difference
+  }
+  __syncthreads();
+  const unsigned int target = target_s;
+  if ((int)threadIdx.x < p.world && (int)threadIdx.x != p.rank) {
+    const unsigned int* mine = reinterpret_cast<const unsigned int*>(p.peer_sig[p.rank]) + kPeerFusedSlot + threadIdx.x;
+    const unsigned long long t0 = globaltimer_ns();
+    for (;;) {
+      unsigned int v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if ((int)(v - target) >= 0) break;
+      const unsigned long long dt = globaltimer_ns() - t0;
+      if (dt > kWaitCheckNs && dt > *(volatile unsigned long long*)&g_fp8imma_wait_limit_ns) {
+        atomicCAS(&g_fp8imma_device_error, 0u, ERR_WAIT_PEER);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 template <int AT, int FMT>
 __global__ void __launch_bounds__(kDecMaxThreads, 1)
     decode_kernel(const __grid_constant__ GemvParams p, const __grid_constant__ CUtensorMap tm_full,
@@ -692,6 +764,7 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
     if (S > 1) sum += recv[(cc * kDecRows + m) * 8 + f];
     dec_store(p, n, m, sum, sc_s[8 * cc + j], cs_s[8 * cc + j], rg_s[m]);
   }
+  if (p.world > 1) dec_peer_publish(p, n0 + own_lo * 8, min(p.N, n0 + own_hi * 8));
   DEC_TRACE(8);
 #ifdef FP8IMMA_TRACE
   if (p.trace && threadIdx.x == 0) {
@@ -888,7 +961,8 @@ static bool decode_plan(int M, int N, int K, int a_bytes, int sms, DecodeCfg* ou
 bool decode_applicable(const GemvParams& p, int a_type, int fmt) {
   if (g_decode_mode.load() == 0) return false;
   if (fmt != 0 && fmt != 1) return false;  // int8-exact formats (E4M3 table, E5M2)
-  if (p.world > 1) return false;
+  // several ranks: the fused gather needs the col-major layout
+  if (p.world > 1 && (p.out_row_major || p.world > 8)) return false;
   DecodeCfg cfg;
   size_t smem;
   // rows quantised by the pre-pass arrive as int8 (half the shared memory)
@@ -945,14 +1019,27 @@ cudaError_t launch_decode(const GemvParams& p_in, int a_type, int fmt, cudaStrea
                       esz == 1 ? kDecQBox : kDecABox, (uint32_t)cfg.arows, false);
   if (e != cudaSuccess) return e;
   switch (a_type * 8 + fmt) {
-    case A_F16 * 8 + 0: return dec_launch<A_F16, FMT_E4M3_REF>(p, tf, ts, ta, cfg, smem, stream);
-    case A_F16 * 8 + 1: return dec_launch<A_F16, FMT_E5M2>(p, tf, ts, ta, cfg, smem, stream);
-    case A_BF16 * 8 + 0: return dec_launch<A_BF16, FMT_E4M3_REF>(p, tf, ts, ta, cfg, smem, stream);
-    case A_BF16 * 8 + 1: return dec_launch<A_BF16, FMT_E5M2>(p, tf, ts, ta, cfg, smem, stream);
-    case A_S8 * 8 + 0: return dec_launch<A_S8, FMT_E4M3_REF>(p, tf, ts, ta, cfg, smem, stream);
-    case A_S8 * 8 + 1: return dec_launch<A_S8, FMT_E5M2>(p, tf, ts, ta, cfg, smem, stream);
+    case A_F16 * 8 + 0: e = dec_launch<A_F16, FMT_E4M3_REF>(p, tf, ts, ta, cfg, smem, stream); break;
+    case A_F16 * 8 + 1: e = dec_launch<A_F16, FMT_E5M2>(p, tf, ts, ta, cfg, smem, stream); break;
+    case A_BF16 * 8 + 0: e = dec_launch<A_BF16, FMT_E4M3_REF>(p, tf, ts, ta, cfg, smem, stream); break;
+    case A_BF16 * 8 + 1: e = dec_launch<A_BF16, FMT_E5M2>(p, tf, ts, ta, cfg, smem, stream); break;
+    case A_S8 * 8 + 0: e = dec_launch<A_S8, FMT_E4M3_REF>(p, tf, ts, ta, cfg, smem, stream); break;
+    case A_S8 * 8 + 1: e = dec_launch<A_S8, FMT_E5M2>(p, tf, ts, ta, cfg, smem, stream); break;
     default: return cudaErrorInvalidValue;
   }
+  if (e != cudaSuccess || p.world <= 1) return e;
+  // gathered output: wait for the peers' rows (a programmatic dependent, so
+  // it is resident while the decode kernel still runs)
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(1, 1, 1);
+  lc.blockDim = dim3(32, 1, 1);
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  return cudaLaunchKernelEx(&lc, dec_peer_wait_kernel, p);
 }
 
 cudaError_t launch_decode_rowquant(const GemvParams& p_in, int a_type, int fmt, cudaStream_t stream) {
