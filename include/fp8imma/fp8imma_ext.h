@@ -57,8 +57,11 @@ typedef struct fp8imma_gemm_args {
 // Extended GEMM. No reference counterpart (extends imma_fp8.h:230). On the
 // int8-exact path with act_quant = TENSOR, out F16/COL, no col_scales_f32 it
 // equals fp8imma_launch_imma_fp8_actquant_v4_{f16,bf16} bit for bit.
-// Per-row quantisation and the native path use stream-ordered temporary
-// buffers (cudaMallocAsync on `stream`).
+// Temporaries (per-row scales, int8 / E4M3 copies of the operands on the
+// large-M paths, quantised activation rows) live in per-(device, stream)
+// scratch buffers allocated on the first call that needs them and reused by
+// later calls on that stream; a call captured in a CUDA graph before its
+// buffer exists uses stream-ordered cudaMallocAsync / cudaFreeAsync instead.
 int fp8imma_gemm(const fp8imma_gemm_args* args, void* stream);
 
 // fp8imma_gemm with a fused epilogue after the scales, in fp32 before the
