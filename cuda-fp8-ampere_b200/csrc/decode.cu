@@ -577,16 +577,21 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
   uint8_t* adst = kDirect ? reinterpret_cast<uint8_t*>(aq) : raw;
   const bool producer = warp == cwarps && lane == 0 && G > 0;
   DEC_TRACE(10);
+  if (warp == cwarps && G > 0) {  // the producer warp's lanes initialise the barriers in parallel
+    if (lane < cfg.D) {
+      mbar_init(&full[lane], 1);
+      mbar_init(&empty[lane], G);
+    }
+    if (lane == 31) {
+      mbar_init(recv_bar, 1);
+      mbar_init(act_bar, 1);
+    }
+    fence_barrier_init();
+    __syncwarp();
+  }
   if (producer) {
     prefetch_tensormap(tm);
     prefetch_tensormap(&tm_act);
-    for (int s = 0; s < cfg.D; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], G);
-    }
-    mbar_init(recv_bar, 1);
-    mbar_init(act_bar, 1);
-    fence_barrier_init();
     // a few weight stages (which, with programmatic dependent launch, stream
     // while the previous kernel finishes), then the activation rows, then the
     // rest (measured faster than the rows first: the one burst of every stage
@@ -641,6 +646,18 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
     const bool col_ok = active && col < p.N;
     const uint16_t sb = col_ok ? dec_scale_bits(p, col) : (uint16_t)0;
     const int tid = threadIdx.x;
+    // the epilogue's column scale tables (weight metadata: read before the
+    // dependency wait; stored now so the loads' latency hides behind the
+    // weight stream)
+    if (tid < 64) {
+      float scv = 0.0f, csv = 1.0f;
+      if (tid < 8 * G && n0 + tid < p.N) {
+        scv = __half2float(__ushort_as_half(dec_scale_bits(p, n0 + tid)));
+        if (p.col_scale_f32) csv = p.col_scale_f32[n0 + tid];
+      }
+      sc_s[tid] = scv;
+      cs_s[tid] = csv;
+    }
     const uint16_t inv = col_ok ? inv_scale_bits(sb) : (uint16_t)0x3C00u;
     const bool all_fast = named_bar_and(2, nthr, fast_ok<FMT>(inv));  // CTA-uniform transcode choice
     const uint32_t fs = fast_scale<FMT>(inv);
@@ -652,16 +669,10 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
         pre_ok = dec_pretranscode<FMT, false>(smem_u32(stages), full, cfg.stage_bytes, nst, c, q, lane, fs, inv);
     }
     DEC_TRACE(12);
-    float scv = 0.0f, csv = 1.0f;
-    if (tid < 8 * G && n0 + tid < p.N) {
-      scv = __half2float(__ushort_as_half(dec_scale_bits(p, n0 + tid)));
-      if (p.col_scale_f32) csv = p.col_scale_f32[n0 + tid];
-    }
-    if (p.pdl) pdl_wait();  // per-row scales may come from the previous kernel
-    if (tid < 64) {
-      sc_s[tid] = scv;
-      cs_s[tid] = csv;
-    }
+    // per-row scales may come from the previous kernel; without them the
+    // consumers read nothing it writes (the activation rows arrive through the
+    // producer, which waited for it, and the outputs are written after they land)
+    if (p.pdl && (p.row_g || p.row_inv_h)) pdl_wait();
     if (tid < kDecRows) {
       const bool live = tid < p.M;
       rg_s[tid] = live ? (p.row_g ? p.row_g[tid] : p.global_scale) : 0.0f;
