@@ -429,8 +429,10 @@ def main():
                 join()
             e2e_graph.replay()
             torch.cuda.synchronize()
-            e2e_timing = ("CUDA graph of K steps (H2D copy, GEMM, D2H copy per step; consecutive steps on two "
-                          "streams, so one step's copies overlap the other's GEMM)") if world == 1 else (
+            e2e_timing = ("CUDA graph of K steps, each reading its activations from page-locked host memory and "
+                          "writing its result to page-locked host memory (fp8imma_gemm_host_io: on this decode shape "
+                          "the GEMM's own pre-pass and epilogue do the transfers); consecutive steps on two "
+                          "streams") if world == 1 else (
                               "CUDA graph of K steps (H2D copy, GEMM, NVLink gather, D2H copy per step)")
         except Exception:
             e2e_graph = None

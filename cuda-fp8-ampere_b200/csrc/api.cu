@@ -23,6 +23,9 @@ std::atomic<int> g_splitk{0};
 std::atomic<int> g_small_m_max{64};
 std::atomic<int> g_pdl{1};
 thread_local int t_last_path = 0;
+// fp8imma_gemm_host_io on the decode path: mapped host buffers used in place
+thread_local const void* t_a_host = nullptr;
+thread_local void* t_d_host = nullptr;
 #ifdef FP8IMMA_TRACE
 unsigned long long* g_trace = nullptr;  // trace builds only
 int g_dbg = 0;
@@ -77,6 +80,8 @@ static cudaError_t run_int8(GemvParams p, int a_type, int fmt, int group, cudaSt
   if (p.K < 0 || !p.A || !p.B || !p.D || (!p.scale_u16 && !p.scale_tex)) return cudaErrorInvalidValue;
   p.keff_a = p.K - p.K % group;
   p.pdl = g_pdl.load();
+  p.a_host = t_a_host;
+  p.d_host = t_d_host;
 #ifdef FP8IMMA_TRACE
   p.trace = g_trace;
   p.dbg = g_dbg;
@@ -398,6 +403,30 @@ int fp8imma_gemm_host_io(const fp8imma_gemm_args* a, const void* A_host, void* D
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t a_bytes = (size_t)a->M * a->K * (a->a_type == FP8IMMA_A_S8 ? 1 : 2);
   const size_t d_bytes = (size_t)a->M * a->N * 2;
+  // decode shapes: the activation pre-pass reads the page-locked host rows
+  // and the epilogue writes the host result directly (no copy kernels); the
+  // device buffers a->A and a->D are then not both used as staging (a->D
+  // still receives the result, a->A is not written)
+  const void* ah = mapped_host_ptr(A_host);
+  void* dh = const_cast<void*>(mapped_host_ptr(D_host));
+  if (ah && dh && a->path == FP8IMMA_PATH_INT8_EXACT && a->act_quant == FP8IMMA_AQ_TENSOR &&
+      (a->a_type == FP8IMMA_A_F16 || a->a_type == FP8IMMA_A_BF16) && (a->b_format == 0 || a->b_format == 1) &&
+      a->out_type >= 0 && a->out_type <= 1 && a->out_layout >= 0 && a->out_layout <= 1 && (a->K % 16) == 0 &&
+      aligned16(a->A) && aligned16(a->B) && aligned16(ah) && a->col_scales_u16 && a->M <= g_small_m_max.load()) {
+    GemvParams p = base_params(a->A, a->B, a->col_scales_u16, 0ull, a->D, a->M, a->N, a->K, a->global_scale,
+                               a->a_inv_scale);
+    p.out_bf16 = a->out_type;
+    p.out_row_major = a->out_layout;
+    if (gemv_would_decode(p, a->a_type, a->b_format, g_splitk.load()) &&
+        decode_host_direct_ok(p, a->a_type, a->b_format, st)) {
+      t_a_host = ah;
+      t_d_host = dh;
+      const int r = fp8imma_gemm(a, stream);
+      t_a_host = nullptr;
+      t_d_host = nullptr;
+      return r;
+    }
+  }
   cudaError_t e = copy_via_sm(const_cast<void*>(a->A), A_host, a_bytes, st);
   if (e != cudaSuccess) return (int)e;
   int r = fp8imma_gemm(a, stream);

@@ -215,10 +215,9 @@ __device__ __forceinline__ void dec_store(const GemvParams& p, int n, int m, int
   if (p.acc_out) p.acc_out[(size_t)n * p.M + m] = sum;
   const uint16_t o = store_val(bias_act(v, p.bias, n, p.act), p.out_bf16);
   uint16_t* D = static_cast<uint16_t*>(p.D);
-  if (p.out_row_major)
-    D[(size_t)m * p.N + n] = o;
-  else
-    D[(size_t)n * p.M + m] = o;
+  const size_t idx = p.out_row_major ? (size_t)m * p.N + n : (size_t)n * p.M + m;
+  D[idx] = o;
+  if (p.d_host) static_cast<uint16_t*>(p.d_host)[idx] = o;  // the host-buffer entry's output, in place
 }
 
 // One stage of a consumer warp: this lane's 2 x 16 weight bytes, eight
@@ -969,6 +968,15 @@ static bool decode_plan(int M, int N, int K, int a_bytes, int sms, DecodeCfg* ou
   return true;
 }
 
+bool decode_host_direct_ok(const GemvParams& p, int a_type, int fmt, cudaStream_t stream) {
+  if (a_type == A_S8 || p.M < kDecPrepassM || p.no_alloc || p.world > 1 || !decode_applicable(p, a_type, fmt))
+    return false;
+  DecodeCfg cfg;
+  size_t smem;
+  return decode_plan(p.M, p.N, p.K, 1, num_sms_current(), &cfg, &smem) &&
+         stream_scratch_ready(stream, (size_t)p.M * p.K, 1);
+}
+
 bool decode_applicable(const GemvParams& p, int a_type, int fmt) {
   if (g_decode_mode.load() == 0) return false;
   if (fmt != 0 && fmt != 1) return false;  // int8-exact formats (E4M3 table, E5M2)
@@ -983,8 +991,11 @@ bool decode_applicable(const GemvParams& p, int a_type, int fmt) {
 
 cudaError_t launch_decode(const GemvParams& p_in, int a_type, int fmt, cudaStream_t stream) {
   GemvParams p = p_in;
+  if (p.a_host && (a_type == A_S8 || p.M < kDecPrepassM || p.no_alloc)) return cudaErrorNotSupported;
   if (a_type != A_S8 && p.M >= kDecPrepassM && !p.no_alloc) {
     void* aq = stream_scratch(stream, (size_t)p.M * p.K, 1);
+    if (!aq && p.a_host) return cudaErrorNotSupported;  // (the pre-pass is what reads the host rows)
+    const void* a_src = p.a_host ? p.a_host : p.A;
     if (aq) {
       const size_t total = (size_t)p.M * (p.K >> 3);
       cudaLaunchConfig_t lc = {};
@@ -997,9 +1008,9 @@ cudaError_t launch_decode(const GemvParams& p_in, int a_type, int fmt, cudaStrea
       lc.attrs = attr;
       lc.numAttrs = 1;
       cudaError_t e = a_type == A_BF16
-                          ? cudaLaunchKernelEx(&lc, dec_quant_kernel<A_BF16>, p.A, p.M, p.K, p.a_inv_h, p.row_inv_h,
+                          ? cudaLaunchKernelEx(&lc, dec_quant_kernel<A_BF16>, a_src, p.M, p.K, p.a_inv_h, p.row_inv_h,
                                                static_cast<int8_t*>(aq))
-                          : cudaLaunchKernelEx(&lc, dec_quant_kernel<A_F16>, p.A, p.M, p.K, p.a_inv_h, p.row_inv_h,
+                          : cudaLaunchKernelEx(&lc, dec_quant_kernel<A_F16>, a_src, p.M, p.K, p.a_inv_h, p.row_inv_h,
                                                static_cast<int8_t*>(aq));
       if (e != cudaSuccess) return e;
       p.A = aq;

@@ -43,6 +43,11 @@ struct GemvParams {
   unsigned int epoch;                       // 0: counted on the device
   unsigned long long peer_rows[8];          // this rank's output slice inside each rank's full output
   unsigned long long peer_sig[8];           // each rank's signal pad (u32 counters, epoch at kPeerEpochSlot)
+  // host-buffer entry on the decode path: device addresses of page-locked
+  // host activations (read by the activation pre-pass) and host output
+  // (written by the epilogue beside D); null otherwise
+  const void* a_host;
+  void* d_host;
   unsigned long long* trace;        // FP8IMMA_TRACE builds only: per-CTA phase timestamps
   int dbg;                          // FP8IMMA_TRACE builds only: decode kernel experiment switches
 };
@@ -103,6 +108,14 @@ int num_sms_current();
 // Small-M split-K kernel (requires K % 16 == 0, 16-byte aligned A/B rows).
 // splits = 0 picks the K split from the shape.
 cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaStream_t stream);
+// launch_gemv_s8 with these arguments would run the decode kernel
+bool gemv_would_decode(const GemvParams& p, int a_type, int fmt, int splits);
+// the decode kernel would read the activations through its pre-pass (whose
+// scratch already exists on `stream`): host activations / outputs can be used
+// in place (GemvParams::a_host, d_host)
+bool decode_host_direct_ok(const GemvParams& p, int a_type, int fmt, cudaStream_t stream);
+// a per-stream scratch buffer of at least `bytes` already exists (no allocation)
+bool stream_scratch_ready(cudaStream_t stream, size_t bytes, int tag);
 // whether the last launch_gemv_s8 on this thread ran the balanced decode kernel
 bool gemv_last_used_decode();
 int gemv_pick_splits(int N, int K, int mchunks, int num_sms);

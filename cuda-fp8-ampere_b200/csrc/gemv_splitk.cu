@@ -1018,14 +1018,20 @@ static cudaError_t launch_gemv_impl(GemvParams p, int a_type, int fmt, int split
 thread_local bool t_used_decode = false;
 bool gemv_last_used_decode() { return t_used_decode; }
 
+bool gemv_would_decode(const GemvParams& p, int a_type, int fmt, int splits) {
+  return splits == 0 && g_stream_k.load() != 2 && decode_applicable(p, a_type, fmt);
+}
+
 cudaError_t launch_gemv_s8(GemvParams p, int a_type, int fmt, int splits, cudaStream_t stream) {
   // shapes that fit one balanced wave (decode sizes) take the one-CTA-per-SM kernel
-  t_used_decode = splits == 0 && g_stream_k.load() != 2 && decode_applicable(p, a_type, fmt);
+  t_used_decode = gemv_would_decode(p, a_type, fmt, splits);
   if (t_used_decode) {
     const cudaError_t e = launch_decode(p, a_type, fmt, stream);
     if (e != cudaErrorNotSupported) return e;
     t_used_decode = false;  // the shape needs the pre-pass, which had no scratch: split-K kernels instead
   }
+  // host buffers in place are only ever handed to the decode kernel
+  if (p.a_host || p.d_host) return cudaErrorNotSupported;
   // Every column tile stages and quantises its own copy of the activations;
   // when that repeated work is large (many tiles, M >= 16) the activations are
   // quantised once by a pre-pass and the kernel copies int8 rows instead.

@@ -53,6 +53,14 @@ std::map<std::tuple<int, cudaStream_t, int>, std::pair<void*, size_t>> g_scratch
 std::vector<void*> g_scratch_retired;
 }  // namespace
 
+bool stream_scratch_ready(cudaStream_t stream, size_t bytes, int tag) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  auto it = g_scratch.find(std::make_tuple(dev, stream, tag));
+  return it != g_scratch.end() && it->second.second >= bytes;
+}
+
 void* stream_scratch(cudaStream_t stream, size_t bytes, int tag, bool* fresh) {
   if (fresh) *fresh = false;
   int dev = 0;

@@ -74,7 +74,12 @@ int fp8imma_gemm_epilogue(const fp8imma_gemm_args* args, const float* bias, int 
 // copy) into args->A, runs fp8imma_gemm, and copies args->D (M x N outputs)
 // back into D_host, all queued on `stream` (the call returns before the
 // copies finish; synchronise the stream before reading D_host). args->A and
-// args->D are the caller's device staging buffers.
+// args->D are the caller's device staging buffers. On the decode shapes
+// (int8-exact path, per-tensor quantisation, fp16 / bf16 activations, M small
+// enough for the balanced decode kernel) with page-locked A_host and D_host,
+// once the stream has run one such call, the kernels read A_host and write
+// D_host in place instead (no copies): args->D still receives the result,
+// args->A is then not written.
 int fp8imma_gemm_host_io(const fp8imma_gemm_args* args, const void* A_host, void* D_host, void* stream);
 
 // Weight quantiser (no reference counterpart beyond an approximate per-tensor
