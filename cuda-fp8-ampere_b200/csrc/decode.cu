@@ -833,8 +833,7 @@ __global__ void __launch_bounds__(256) dec_rowquant_kernel(const void* __restric
   uint2* out = reinterpret_cast<uint2*>(Aq + (size_t)m * K);
   const int items = K >> 3;
   float amax = 0.0f;
-  for (int i = threadIdx.x; i < items; i += blockDim.x) {
-    uint4 v = row[i];
+  auto absmax8 = [&](const uint4& v) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -842,7 +841,20 @@ __global__ void __launch_bounds__(256) dec_rowquant_kernel(const void* __restric
       const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
       amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
     }
+  };
+  // the first kKeep vectors of each thread stay in registers for the
+  // quantisation (one read of the row for K <= 8192), the rest is read again
+  constexpr int kKeep = 4;
+  uint4 keep[kKeep];
+#pragma unroll
+  for (int j = 0; j < kKeep; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < items) {
+      keep[j] = row[i];
+      absmax8(keep[j]);
+    }
   }
+  for (int i = threadIdx.x + kKeep * blockDim.x; i < items; i += blockDim.x) absmax8(row[i]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
@@ -862,8 +874,7 @@ __global__ void __launch_bounds__(256) dec_rowquant_kernel(const void* __restric
   }
   __syncthreads();
   const uint32_t ainv2 = inv_s;
-  for (int i = threadIdx.x; i < items; i += blockDim.x) {  // second read: L1 / L2 resident
-    uint4 v = row[i];
+  auto quant8 = [&](uint4 v, int i) {
     if (AT == A_BF16) {
       v.x = bf16x2_to_f16x2(v.x);
       v.y = bf16x2_to_f16x2(v.y);
@@ -871,7 +882,13 @@ __global__ void __launch_bounds__(256) dec_rowquant_kernel(const void* __restric
       v.w = bf16x2_to_f16x2(v.w);
     }
     out[i] = make_uint2(quant4_f16(v.x, v.y, ainv2), quant4_f16(v.z, v.w, ainv2));
+  };
+#pragma unroll
+  for (int j = 0; j < kKeep; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < items) quant8(keep[j], i);
   }
+  for (int i = threadIdx.x + kKeep * blockDim.x; i < items; i += blockDim.x) quant8(row[i], i);  // L1 / L2 resident
 }
 
 std::atomic<int> g_decode_mode{1};
