@@ -292,12 +292,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) o[j] = (uint16_t)(pk[j >> 1] >> (16 * (j & 1)));
         const int mcount = min(32, p.M - mbase);
-#ifdef FP8IMMA_TC_EPI_DBG
-        if (FP8IMMA_TC_EPI_DBG == 1) {
-          if (o[0] == 0x1234u && o[31] == 0x9u) D[0] = 1;
-          continue;
-        }
-#endif
         if (p.out_row_major) {
           _Pragma("unroll") for (int j = 0; j < 32; ++j) if (j < mcount) D[(size_t)(mbase + j) * p.N + n] = o[j];
         } else {
@@ -808,17 +802,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           __syncwarp();
           uint32_t pk[16];
           tc_epi_pack<KIND>(r, mbase, cs, cs2, p, nok ? n : 0, pk);
-#if defined(FP8IMMA_TC_EPI_DBG) && FP8IMMA_TC_EPI_DBG == 5
-          _Pragma("unroll") for (int w2 = 0; w2 < 16; ++w2) pk[w2] = (r[2 * w2] & 0xFFFFu) | (r[2 * w2 + 1] << 16);
-#endif
-#if defined(FP8IMMA_TC_EPI_DBG) && FP8IMMA_TC_EPI_DBG == 6
-          {
-            uint32_t x = 0;
-            _Pragma("unroll") for (int w2 = 0; w2 < 16; ++w2) x ^= pk[w2] * (w2 + 1);
-            if (x == 0x12345679u) D[0] = 1;
-            continue;
-          }
-#endif
           uint4* row4 = reinterpret_cast<uint4*>(st + lane * 16);
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) row4[v4] = make_uint4(pk[4 * v4], pk[4 * v4 + 1], pk[4 * v4 + 2], pk[4 * v4 + 3]);
@@ -840,12 +823,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           continue;
         }
         if (!nok || mbase >= p.M) continue;
-#ifdef FP8IMMA_TC_EPI_DBG
-        if (FP8IMMA_TC_EPI_DBG == 2) {
-          if (r[0] == 0x12345678u && r[31] == 0x9u) static_cast<uint16_t*>(p.D)[0] = 1;
-          continue;
-        }
-#endif
         if (p.splits > 1) {  // raw accumulators of this K split; tc_splitk_reduce_kernel finishes
           uint32_t* dst = p.ws + ((size_t)split * p.N + n) * p.M + mbase;
           const int mc = min(32, p.M - mbase);
@@ -870,12 +847,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) o[j] = (uint16_t)(pk[j >> 1] >> (16 * (j & 1)));
         const int mcount = min(32, p.M - mbase);
-#ifdef FP8IMMA_TC_EPI_DBG
-        if (FP8IMMA_TC_EPI_DBG == 1) {
-          if (o[0] == 0x1234u && o[31] == 0x9u) D[0] = 1;
-          continue;
-        }
-#endif
         if (p.out_row_major) {
           _Pragma("unroll") for (int j = 0; j < 32; ++j) if (j < mcount) D[(size_t)(mbase + j) * p.N + n] = o[j];
         } else {
