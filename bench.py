@@ -17,8 +17,14 @@ value       whole-job algorithmic GB/s (N*K + 4N + 2MK + 2MN bytes per GEMM),
             by rotating > 2x L2 worth of weight copies.
 e2e         the same metric through the library's host-buffer entry
             (fp8imma_gemm_host_io via fp8imma_ext.imma_fp8_gemm(a_host=,
-            out_host=)): every step copies that step's pinned host
-            activations in and the result out, around the GEMM.
+            out_host=)): every step reads that step's pinned host
+            activations and writes the result to pinned host memory (on the
+            decode shape the GEMM's own pre-pass and epilogue do the
+            transfers); one GPU: consecutive steps alternate between two
+            streams.
+metric_points  the metric's other points on one GPU (decode M=1, decode M=16
+            with per-row quantisation, square 4096^3), each with its own
+            roofline and clock record.
 --impl reference: the reference's own arithmetic on the host cores (the CPU
             oracle, all threads; the reference has no CPU implementation of
             its own), same workload, metric and unit.
