@@ -146,3 +146,16 @@ def test_decode_equals_split_k_kernel_graph_replay(decode_on, M, pdl):
         for o in outs:
             assert torch.equal(o.view(torch.int16), D_ref.view(torch.int16))
     assert L.fp8imma_device_error(1) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(4, 512, 12288), (16, 1000, 12288)])
+def test_decode_rowquant_long_rows(decode_on, M, N, K):
+    """Per-row quantisation with rows longer than the pre-pass keeps in
+    registers (K > 8192: the rest of the row is read a second time)."""
+    A, B, s, sig = inputs(M, N, K, seed=K + M)
+    D, acc, path = _gemm(A, B, s, sig, M, N, K, row_quant=True)
+    assert path == DECODE_PATH
+    D_o, acc_o = O.gemm_ex(A, B, s, row_quant=True, col_scale_f32=sig, global_scale=0.05, a_inv_scale=20.0,
+                           nthreads=16)
+    assert (acc.cpu().numpy() == acc_o).all()
+    assert bits_equal(to_np_bits(D), D_o).all()
