@@ -82,7 +82,9 @@ def test_rank_that_never_joins_ends_rendezvous_with_error():
 
 def _dying_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    # a timeout long enough for both ranks to start on a loaded machine; the
+    # survivor learns of the dead peer from its closed connection, not from it
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
     M, N, K = 4, 32 * world, 32
     rng = np.random.default_rng(0)
     A = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float16))
@@ -120,4 +122,4 @@ def test_rank_dying_between_steps_fails_the_next_collective():
     assert procs[-1].exitcode == 3
     rank, kind, dt = q.get(timeout=5)
     assert rank == 0 and kind != "completed", (rank, kind)
-    assert dt < 60
+    assert dt < 45
