@@ -576,7 +576,7 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
   uint8_t* adst = kDirect ? reinterpret_cast<uint8_t*>(aq) : raw;
   const bool producer = warp == cwarps && lane == 0 && G > 0;
   DEC_TRACE(10);
-  if (warp == cwarps && G > 0) {  // the producer warp's lanes initialise the barriers in parallel
+  if (warp == cwarps && G > 0) {  // the producer warp's lanes initialise the barriers in parallel, then
     if (lane < cfg.D) {
       mbar_init(&full[lane], 1);
       mbar_init(&empty[lane], G);
@@ -586,19 +586,19 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
       mbar_init(act_bar, 1);
     }
     fence_barrier_init();
+    if (lane == 0) prefetch_tensormap(tm);
     __syncwarp();
-  }
-  if (producer) {
-    prefetch_tensormap(tm);
-    prefetch_tensormap(&tm_act);
-    // a few weight stages (which, with programmatic dependent launch, stream
-    // while the previous kernel finishes), then the activation rows, then the
-    // rest (measured faster than the rows first: the one burst of every stage
-    // at once delayed the whole stream)
-    for (int i = 0; i < early; ++i) {  // the ring is empty: no waits
+    // the first weight stages, requested by the lanes at once (with
+    // programmatic dependent launch they stream while the previous kernel
+    // finishes); the activation rows follow (measured faster than the rows
+    // first), then the rest of a recycling ring
+    for (int i = lane; i < early; i += 32) {  // the ring is empty: no waits
       mbar_arrive_expect_tx(&full[i], wbytes);
       tma_load_2d(stages + i * cfg.stage_bytes, tm, &full[i], k0 + i * kDecBoxK, n0);
     }
+  }
+  if (producer) {
+    prefetch_tensormap(&tm_act);
     if (!p.pdl) {
       mbar_arrive_expect_tx(act_bar, (uint32_t)(nbox * cfg.arows * abox_bytes));
       for (int j = 0; j < nbox; ++j) tma_load_2d(adst + j * abox_slot, &tm_act, act_bar, (k0 + j * abox_k) * esz, 0);
