@@ -621,15 +621,17 @@ __global__ void __launch_bounds__(kDecMaxThreads, 1)
     for (int j = 0; j < 2; ++j) acc[h][j][0] = acc[h][j][1] = acc[h][j][2] = acc[h][j][3] = 0;
 
   if (warp == cwarps) {
-    // ---- TMA producer: the activation rows (after the previous kernel when
-    // launched as a programmatic dependent), then the remaining weight stages
+    // ---- TMA producer warp: the activation rows (after the previous kernel
+    // when launched as a programmatic dependent), then the remaining weight
+    // stages of a recycling ring
+    if (G > 0 && p.pdl) {  // the activation boxes, one per lane, after the previous kernel
+      pdl_wait();  // activations may come from the previous kernel
+      if (lane == 0) mbar_arrive_expect_tx(act_bar, (uint32_t)(nbox * cfg.arows * abox_bytes));
+      __syncwarp();
+      for (int j = lane; j < nbox; j += 32) tma_load_2d(adst + j * abox_slot, &tm_act, act_bar, (k0 + j * abox_k) * esz, 0);
+    }
     if (producer) {
       const int D = cfg.D;
-      if (p.pdl) {
-        pdl_wait();  // activations may come from the previous kernel
-        mbar_arrive_expect_tx(act_bar, (uint32_t)(nbox * cfg.arows * abox_bytes));
-        for (int j = 0; j < nbox; ++j) tma_load_2d(adst + j * abox_slot, &tm_act, act_bar, (k0 + j * abox_k) * esz, 0);
-      }
       for (int i = early; i < nst; ++i) {
         const int s = i % D;
         if (i >= D && !mbar_wait(&empty[s], ((i / D) & 1) ^ 1u, ERR_WAIT_EMPTY)) break;
