@@ -106,6 +106,9 @@ def _dying_worker(rank, world, port, q):
         q.put((rank, "completed", time.time() - t0))
     except Exception as e:
         q.put((rank, type(e).__name__, time.time() - t0))
+    # os._exit skips the queue's feeder thread: flush the report first
+    q.close()
+    q.join_thread()
     os._exit(0)
 
 
