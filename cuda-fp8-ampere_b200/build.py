@@ -58,6 +58,11 @@ def build_lib(force: bool = False, extra_flags: list[str] | None = None) -> str:
     """Compile every .cu for sm_100a and link libfp8imma.so."""
     os.makedirs(OBJ, exist_ok=True)
     hdrs = _headers()
+    # objects built with other flags (or another nvcc) are stale whatever their age
+    stamp = os.path.join(OBJ, "flags.txt")
+    flags = " ".join([NVCC] + ARCH + NVCC_FLAGS + (extra_flags or []))
+    if not os.path.exists(stamp) or open(stamp).read() != flags:
+        force = True
     objs, jobs = [], []
     for src in CU_SOURCES:
         s = os.path.join(CSRC, src)
@@ -67,8 +72,13 @@ def build_lib(force: bool = False, extra_flags: list[str] | None = None) -> str:
             jobs.append([NVCC] + ARCH + NVCC_FLAGS + (extra_flags or []) + ["-c", s, "-o", o])
     with cf.ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as ex:
         list(ex.map(_run, jobs))
-    if force or jobs or not _newer(LIB, objs):
+    relink = force or bool(jobs) or not _newer(LIB, objs)
+    if relink:
         _run([NVCC] + ARCH + ["-shared", "-Xcompiler", "-fPIC", "-o", LIB] + objs + ["-lcudart"])
+    with open(stamp, "w") as f:
+        f.write(flags)
+    sys.stderr.write("libfp8imma.so: %d of %d sources compiled, %s\n"
+                     % (len(jobs), len(CU_SOURCES), "relinked" if relink else "up to date"))
     return LIB
 
 
